@@ -1,0 +1,392 @@
+"""Benchmark of the B200 Q8_0 quantized linear (decode path, HBM-bound).
+
+Workload (decode rows): the four projection shapes of the shape
+sweep -- fused QKV (2048->6144), O (2048->2048), fused gate+up (2048->12288) and
+down (6144->2048) -- at M = 1, for 28 distinct layers of Q8_0 weights (the depth of
+the 2B decoder).  One step = one pass over all 28 x 4 = 112 projections, i.e. the
+Q8_0 linear work of one decode token.  The 1.62 GB of weights is 13x the 126 MB L2,
+so no step reads weights from L2 that an earlier one left there.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Output: one JSON line (rank 0).  ``value`` = algorithmic bytes / device time
+(N*K*34/32 + 4*M*K + 4*M*N per projection) summed over ranks, in TB/s.
+``e2e`` = the same metric through the C ABI with the step's activations copied from
+pinned host memory and its outputs read back every step.  ``--impl reference`` times
+the candle-CPU restatement (oracle/, the reference's own algorithm) on host cores.
+Multi-GPU: every rank runs its own replica of the workload (independent decode
+streams, no collective on the data path), so scaling is weak.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import ctypes
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SHAPES = [("qkv", 2048, 6144), ("o", 2048, 2048), ("gate_up", 2048, 12288), ("down", 6144, 2048)]
+LAYERS = 28
+METRIC = "Q8_0 matmul achieved HBM TB/s (decode GEMV, M=1)"
+
+
+def algorithmic_bytes(m: int, k: int, n: int) -> int:
+    return n * k * 34 // 32 + 4 * m * k + 4 * m * n
+
+
+def load_peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<name> (or None)."""
+    p = os.path.join(ROOT, "profiles", name)
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples for one GPU during the timed region."""
+
+    FIELDS = ("pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, pci_bus: int):
+        self.pci_bus = pci_bus
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        for row in csv.reader(io.StringIO(out)):
+            if len(row) < 9:
+                continue
+            row = [c.strip() for c in row]
+            try:
+                bus = int(row[0].split(":")[1], 16)
+            except (IndexError, ValueError):
+                continue
+            if bus != self.pci_bus:
+                continue
+            try:
+                sm.append(float(row[1]))
+                smax.append(float(row[2]))
+            except ValueError:
+                continue
+            for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
+                                 row[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU legs
+def cpu_run(threads: int, budget_s: float, layers: int = 2, min_steps: int = 1):
+    """candle-CPU restatement timed on host cores over the same projection shapes (M=1).
+
+    Returns (TB/s, projections timed, seconds, description)."""
+    import oracle
+    from talechime_b200 import synth
+
+    oracle.build()
+    rng = np.random.default_rng(0)
+    ws = [[(synth.q8_0_blocks(rng, n, k), k, n) for (_, k, n) in SHAPES] for _ in range(layers)]
+    xs = {k: rng.standard_normal((1, k), dtype=np.float32) for (_, k, _) in SHAPES}
+    oracle.matmul(xs[2048], ws[0][1][0], 2048, threads=threads)  # warm-up
+    t0 = time.perf_counter()
+    done, nbytes, i = 0, 0, 0
+    while True:
+        layer = ws[(i // len(SHAPES)) % layers]
+        w, k, n = layer[i % len(SHAPES)]
+        oracle.matmul(xs[k], w, n, threads=threads)
+        nbytes += algorithmic_bytes(1, k, n)
+        done += 1
+        i += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s and done >= min_steps:
+            break
+    return nbytes / el / 1e12, done, el
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    # each step: one projection (cycling through the 4 shapes of 2 layers), bounded so
+    # that --steps K finishes in minutes
+    import oracle
+    from talechime_b200 import synth
+
+    oracle.build()
+    rng = np.random.default_rng(0)
+    layers = 2
+    ws = [[(synth.q8_0_blocks(rng, n, k), k, n) for (_, k, n) in SHAPES] for _ in range(layers)]
+    xs = {k: rng.standard_normal((1, k), dtype=np.float32) for (_, k, _) in SHAPES}
+    seq = [ws[li][si] for li in range(layers) for si in range(len(SHAPES))]
+    for i in range(args.warmup):
+        w, k, n = seq[i % len(seq)]
+        oracle.matmul(xs[k], w, n, threads=threads)
+    nbytes = 0
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        w, k, n = seq[i % len(seq)]
+        oracle.matmul(xs[k], w, n, threads=threads)
+        nbytes += algorithmic_bytes(1, k, n)
+    el = time.perf_counter() - t0
+    value = nbytes / el / 1e12
+    sample = (f"{args.steps} projections (cycling qkv/o/gate_up/down of {layers} layers, M=1) "
+              f"with the candle-CPU restatement (oracle/q8_0_oracle.c, scalar vec_dot order)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3 / max(args.steps, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint8->f32",
+        "data": "synthetic", "config": config_block(world),
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_block(world: int) -> dict:
+    return {"workload": "configs[1] decode rows: qkv 2048->6144, o 2048->2048, gate_up 2048->12288, "
+                        "down 6144->2048 at M=1, x 28 layers (one decode token of Q8_0 linears)",
+            "m": 1, "layers": LAYERS, "weight_bytes_per_step": sum(algorithmic_bytes(0, k, n) for _, k, n in SHAPES) * LAYERS,
+            "l2": "inputs larger than L2: 1.62 GB of distinct weights per step (13x the 126 MB L2)",
+            "parallelism": f"replicas x{world}"}
+
+
+# --------------------------------------------------------------------------- GPU leg
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds for the cpu_baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="layer copies (28 = the benchmark; fewer only for small profiling captures)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    from talechime_b200 import QMatMul, _lib, build
+
+    if rank == 0 or world == 1:
+        build.build()
+    if world > 1:
+        dist.barrier()
+    L = _lib.lib()
+
+    # weights: 28 layers x 4 shapes, random Q8_0 blocks generated on the device
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    mats = []
+    for _ in range(args.layers):
+        for name, k, n in SHAPES:
+            nb = k // 32
+            blocks = torch.empty((n, nb, 34), dtype=torch.uint8, device=dev)
+            qs = torch.randint(-127, 128, (n, nb, 32), generator=gen, device=dev, dtype=torch.int8)
+            d = (torch.randn((n, nb), generator=gen, device=dev).abs() * (0.02 / 127.0)).half()
+            blocks[:, :, 2:] = qs.view(torch.uint8)
+            blocks[:, :, :2] = d.view(torch.uint8).view(n, nb, 2)
+            mats.append(QMatMul.from_gguf_blocks(blocks, n, k, device=dev))
+            del blocks, qs, d
+    torch.cuda.synchronize()
+    xs = {k: torch.randn((1, k), generator=gen, device=dev) for _, k, _ in SHAPES}
+    ys = [torch.empty((1, m.n), device=dev) for m in mats]
+    stream = torch.cuda.current_stream(dev)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    handles = [m.handle for m in mats]
+    xptr = [ctypes.c_void_p(xs[m.k].data_ptr()) for m in mats]
+    yptr = [ctypes.c_void_p(y.data_ptr()) for y in ys]
+    fwd = L.q8lin_forward
+
+    def step():
+        for h, xp, yp in zip(handles, xptr, yptr):
+            st = fwd(h, xp, yp, 1, sptr)
+            if st:
+                _lib.check(st)
+
+    bytes_per_step = sum(algorithmic_bytes(1, k, n) for _, k, n in SHAPES) * args.layers
+    launches_per_step = len(mats)
+
+    # Capture one step in a CUDA graph: the device-side timing then measures the
+    # kernels back to back without host launch gaps (host cost is in e2e).
+    graph = torch.cuda.CUDAGraph()
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(dev)
+    sampler = ClockSampler(props.pci_bus_id)
+    sampler.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * bytes_per_step / (ms * 1e-3) / 1e12
+
+    # ---- e2e: through the C ABI, activations from pinned host memory, outputs back
+    if args.no_e2e:
+        line = {"metric": METRIC, "value": value, "unit": "TB/s", "ms_per_step": ms, "layers": args.layers,
+                "clocks": clocks, "note": "profiling run (--no-e2e); not a bench line"}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        del graph
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    xin = {k: torch.randn((1, k), generator=gen, device=dev).cpu().pin_memory() for _, k, _ in SHAPES}
+    yhost = torch.empty(sum(y.numel() for y in ys), dtype=torch.float32).pin_memory()
+    yall = torch.cat([y.reshape(-1) for y in ys])
+    h2d = sum(v.numel() * 4 for v in xin.values())
+    d2h = yhost.numel() * 4
+    ycat_views = []
+    off = 0
+    for y in ys:
+        ycat_views.append(yall[off:off + y.numel()])
+        off += y.numel()
+    yptr2 = [ctypes.c_void_p(v.data_ptr()) for v in ycat_views]
+
+    def e2e_step():
+        for k, v in xin.items():
+            xs[k].copy_(v, non_blocking=True)
+        for h, xp, yp in zip(handles, xptr, yptr2):
+            st = fwd(h, xp, yp, 1, sptr)
+            if st:
+                _lib.check(st)
+        yhost.copy_(yall, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(args.warmup):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    e2e_steps = max(1, args.steps // 4)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * bytes_per_step / (e2e_ms * 1e-3) / 1e12
+
+    peak, peak_kind = load_peaks()
+    achieved_gbs = (bytes_per_step / launches_per_step) / (ms * 1e-3 / launches_per_step) / 1e9
+    traffic = profile_traffic("gemv_q8_0_decode.txt")
+    line = {
+        "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8xint8->f32", "data": "synthetic",
+        "config": config_block(world),
+        "tokens_per_s_linears_only": world * 1e3 / ms,
+        "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
+                     "frac": achieved_gbs / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                     if peak_kind == "measured" else "fallback 6.65 TB/s",
+                     "traffic": traffic, "kernel": "gemv_q8_0_kernel<1>",
+                     "bytes_per_launch": bytes_per_step / launches_per_step},
+        "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms, "steps": e2e_steps,
+                "path": "q8lin_forward (C ABI via ctypes) x112, pinned H2D of x, D2H of y, stream sync per step"},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        v, done, el = cpu_run(threads, args.cpu_budget)
+        line["cpu_baseline"] = {
+            "value": v, "unit": "TB/s", "cores": threads, "kind": "port",
+            "sample": f"{done} projections (qkv/o/gate_up/down of 2 layers, M=1) in {el:.1f} s with the "
+                      f"candle-CPU restatement (oracle/q8_0_oracle.c)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,116 @@
+/*
+ * q8lin.h -- C ABI of the B200 (sm_100a) Q8_0 quantized linear.
+ *
+ * Drop-in for the Q8_0 projection path of talechime's VoxCPM BaseLM:
+ *   Weights::linear keeps a Q8_0 GGUF tensor as QMatMul::QTensor(Arc<QTensor>)
+ *     (crates/voxcpm/src/weights.rs:98-117, Q8_0 test at :103-104)
+ *   Linear::forward flattens x to [rows, in] and calls QMatMul::forward
+ *     (crates/voxcpm/src/weights.rs:213-229; the call itself at :221)
+ *   callers: Transformer::forward q/k/v/o/gate/up/down
+ *     (crates/voxcpm/src/transformer.rs:119-121,146,148-150).
+ * The arithmetic it replaces is candle-core 0.11.0's QMatMul over GgmlDType::Q8_0
+ * (third-party; Cargo.toml:20,94-98).
+ *
+ * Conventions
+ *   - Every function returns an int status (Q8LIN_OK == 0) and never aborts;
+ *     q8lin_last_error() returns the calling thread's message for the last failure.
+ *   - Streams are cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - x / y / workspace are device pointers on the weight's device, 16-byte aligned.
+ *   - q8lin_forward* never synchronizes the host.  q8lin_forward_ws allocates
+ *     nothing; q8lin_forward allocates its workspace on first use for M > 16 (see
+ *     q8lin_reserve_workspace to do that before stream capture).
+ */
+#ifndef Q8LIN_H
+#define Q8LIN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q8LIN_VERSION 1
+#define Q8LIN_QK 32          /* values per Q8_0 block */
+#define Q8LIN_BLOCK_BYTES 34 /* GGUF block: f16 d + int8 qs[32] */
+
+typedef struct q8lin_weight q8lin_weight; /* one Q8_0 projection resident on one GPU */
+typedef void* q8lin_stream_t;             /* cudaStream_t */
+
+enum q8lin_status {
+  Q8LIN_OK = 0,
+  Q8LIN_ERR_INVALID_ARGUMENT = 1, /* null handle/pointer, negative size */
+  Q8LIN_ERR_SHAPE = 2,            /* K % 32 != 0, K mismatch, size beyond limits */
+  Q8LIN_ERR_ALIGNMENT = 3,        /* device pointer not 16-byte aligned */
+  Q8LIN_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed */
+  Q8LIN_ERR_NCCL = 5,             /* a collective failed (tensor-parallel entry points) */
+  Q8LIN_ERR_OUT_OF_MEMORY = 6,
+  Q8LIN_ERR_DEVICE = 7,           /* not a compute-capability 10.0 GPU, or wrong device */
+  Q8LIN_ERR_WORKSPACE = 8         /* caller workspace smaller than q8lin_workspace_size */
+};
+
+/* Library version (Q8LIN_VERSION). */
+int q8lin_version(void);
+/* Message of the calling thread's last failing call ("" if none). */
+const char* q8lin_last_error(void);
+/* Static name of a status code. */
+const char* q8lin_status_string(int status);
+
+/*
+ * Upload and repack one Q8_0 GGUF tensor.
+ * Replaces: Content::tensor(file, name, device) -> QTensor and the
+ *   QMatMul::QTensor(Arc::new(q)) construction (crates/voxcpm/src/weights.rs:100-104).
+ * gguf_blocks: N rows x K/32 blocks of 34 bytes, the tensor's bytes as stored in the
+ *   GGUF file (ggml ne = [K, N]); host or device memory (detected).
+ * Repacks on `device` into per-row [int8 qs[K] | f16 d[K/32] | pad to 16 B] rows.
+ * Synchronizes `stream` before returning (load time, not the hot path).
+ */
+int q8lin_weight_create(const void* gguf_blocks, int64_t n, int64_t k, int device,
+                        q8lin_stream_t stream, q8lin_weight** out);
+/* Free a weight (NULL is a no-op). */
+int q8lin_weight_destroy(q8lin_weight* w);
+/* Logical shape: n = out features, k = in features (candle shape (n, k)). */
+int q8lin_weight_shape(const q8lin_weight* w, int64_t* n, int64_t* k, int* device);
+/* Bytes the repacked weight holds in HBM. */
+int q8lin_weight_device_bytes(const q8lin_weight* w, size_t* bytes);
+/*
+ * Dequantize to f32 [N][K] (device memory).
+ * Replaces: QTensor::dequantize (crates/voxcpm/src/weights.rs:79-80,106).
+ */
+int q8lin_weight_dequantize(const q8lin_weight* w, float* out, q8lin_stream_t stream);
+/* Write the weight back in GGUF block layout (device memory, N*K/32*34 bytes). */
+int q8lin_weight_export_gguf(const q8lin_weight* w, void* out_blocks, q8lin_stream_t stream);
+
+/* Workspace bytes q8lin_forward_ws needs for M rows (0 for M <= 16). */
+size_t q8lin_workspace_size(const q8lin_weight* w, int64_t m);
+
+/*
+ * y[M][N] = x[M][K] . W^T with candle's CPU Q8_0 semantics: every x row is
+ * quantized to Q8_0 blocks (d = amax/127, q = round-half-away(x * (1/d)), d kept
+ * as f16), then y = sum over blocks of f32(isum) * f32(dw) * f32(dx) in f32.
+ * Replaces: QMatMul::forward for QMatMul::QTensor/Q8_0, called at
+ *   crates/voxcpm/src/weights.rs:221 (shape rules as candle's: 2-D [M, K], K == in).
+ * x, y: f32 device memory, row-major, contiguous.  M == 0 is a no-op.
+ * Uses a library-owned workspace per (device, stream) for M > 16.
+ */
+int q8lin_forward(const q8lin_weight* w, const float* x, float* y, int64_t m,
+                  q8lin_stream_t stream);
+/* As q8lin_forward with a caller-provided workspace; allocates nothing. */
+int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
+                     void* workspace, size_t workspace_bytes, q8lin_stream_t stream);
+/* Grow the library-owned workspace of (device, stream) to cover M rows of K columns. */
+int q8lin_reserve_workspace(int device, q8lin_stream_t stream, int64_t m, int64_t k);
+
+/*
+ * Quantize f32 activations x[M][K] to Q8_0 planes on the device: qs int8 [M][K]
+ * and d as f16 bits [M][K/32].  The quantizer every forward path uses (candle's
+ * BlockQ8_0::from_float applied to the lhs rows of its CPU matmul).
+ */
+int q8lin_quantize_rows(const float* x, int64_t m, int64_t k, int8_t* qs, uint16_t* d_f16,
+                        q8lin_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q8LIN_H */

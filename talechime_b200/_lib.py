@@ -1,0 +1,90 @@
+"""ctypes binding of libq8lin.so (the C ABI declared in include/q8lin.h).
+
+The library is loaded from the package directory only.  There is no fallback: if
+it is missing, importing the operator fails with instructions to build it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libq8lin.so")
+
+# Status codes (enum q8lin_status).
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_SHAPE = 2
+ERR_ALIGNMENT = 3
+ERR_CUDA = 4
+ERR_NCCL = 5
+ERR_OUT_OF_MEMORY = 6
+ERR_DEVICE = 7
+ERR_WORKSPACE = 8
+
+# Every symbol the header declares, with (restype, argtypes).
+_c_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+SIGNATURES = {
+    "q8lin_version": (ctypes.c_int, []),
+    "q8lin_last_error": (ctypes.c_char_p, []),
+    "q8lin_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "q8lin_weight_create": (ctypes.c_int, [_c_p, _i64, _i64, ctypes.c_int, _c_p, ctypes.POINTER(_c_p)]),
+    "q8lin_weight_destroy": (ctypes.c_int, [_c_p]),
+    "q8lin_weight_shape": (ctypes.c_int, [_c_p, ctypes.POINTER(_i64), ctypes.POINTER(_i64),
+                                          ctypes.POINTER(ctypes.c_int)]),
+    "q8lin_weight_device_bytes": (ctypes.c_int, [_c_p, ctypes.POINTER(ctypes.c_size_t)]),
+    "q8lin_weight_dequantize": (ctypes.c_int, [_c_p, _c_p, _c_p]),
+    "q8lin_weight_export_gguf": (ctypes.c_int, [_c_p, _c_p, _c_p]),
+    "q8lin_workspace_size": (ctypes.c_size_t, [_c_p, _i64]),
+    "q8lin_forward": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p]),
+    "q8lin_forward_ws": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p, ctypes.c_size_t, _c_p]),
+    "q8lin_reserve_workspace": (ctypes.c_int, [ctypes.c_int, _c_p, _i64, _i64]),
+    "q8lin_quantize_rows": (ctypes.c_int, [_c_p, _i64, _i64, _c_p, _c_p, _c_p]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class Q8LinError(RuntimeError):
+    """A libq8lin call returned a non-zero status (mirrors candle's Error::Msg)."""
+
+    def __init__(self, status: int, message: str):
+        self.status = status
+        name = _status_name(status)
+        super().__init__(f"{name}: {message}")
+
+
+def _status_name(status: int) -> str:
+    try:
+        return lib().q8lin_status_string(status).decode()
+    except Exception:  # library unusable: fall back to the number
+        return f"status {status}"
+
+
+def lib() -> ctypes.CDLL:
+    """Load libq8lin.so once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError(
+                    f"{LIB_PATH} is missing: build it with `python -m talechime_b200.build` "
+                    "(nvcc, sm_100a).  There is no CPU fallback for the Q8_0 linear.")
+            L = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = L
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != OK:
+        msg = lib().q8lin_last_error().decode(errors="replace")
+        raise Q8LinError(status, msg)

@@ -1,0 +1,345 @@
+// C ABI of libq8lin.so (declared in include/q8lin.h): argument checks, weight
+// upload/repack, workspace management and dispatch to the kernels.
+#include <cuda_runtime.h>
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+
+#include "common.cuh"
+#include "internal.h"
+#include "q8lin.h"
+
+namespace q8lin {
+
+static thread_local std::string g_last_error;
+
+int fail(int status, const std::string& msg) {
+  g_last_error = msg;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  const int status = (e == cudaErrorMemoryAllocation) ? Q8LIN_ERR_OUT_OF_MEMORY : Q8LIN_ERR_CUDA;
+  return fail(status, std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+int sm_count(int device) {
+  static int cache[128] = {0};
+  if (device < 0 || device >= 128) return 148;
+  if (cache[device] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0) v = 148;
+    cache[device] = v;
+  }
+  return cache[device];
+}
+
+size_t gemv_smem_bytes(int m, int64_t k);  // gemv.cu
+
+namespace {
+
+constexpr size_t kGemvSmemLimit = 200 * 1024;
+constexpr size_t kAlign = 256;
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+bool use_gemv(int64_t m, int64_t k) {
+  return m >= 1 && m <= kGemvMaxM && gemv_smem_bytes((int)m, k) <= kGemvSmemLimit;
+}
+
+size_t workspace_bytes(int64_t m, int64_t k) {
+  if (m <= 0 || use_gemv(m, k)) return 0;
+  return align_up((size_t)(m * k), kAlign) + align_up((size_t)m * (size_t)(k / kQK) * sizeof(float), kAlign);
+}
+
+// Makes `device` current for the scope and restores the caller's device.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device) {
+    ok_ = cudaGetDevice(&prev_) == cudaSuccess;
+    if (ok_ && prev_ != device) ok_ = cudaSetDevice(device) == cudaSuccess;
+    switched_ = ok_ && prev_ != device;
+  }
+  ~DeviceGuard() {
+    if (switched_) cudaSetDevice(prev_);
+  }
+  bool ok() const { return ok_; }
+
+ private:
+  int prev_ = 0;
+  bool ok_ = false;
+  bool switched_ = false;
+};
+
+int check_device(int device) {
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= count)
+    return fail(Q8LIN_ERR_DEVICE, "device " + std::to_string(device) + " out of range (" +
+                                      std::to_string(count) + " visible)");
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (major != 10 || minor != 0)
+    return fail(Q8LIN_ERR_DEVICE, "libq8lin is built for sm_100a only; device " + std::to_string(device) +
+                                      " is sm_" + std::to_string(major) + std::to_string(minor));
+  return Q8LIN_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct Workspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, Workspace> g_ws;
+
+// Returns a workspace of at least `need` bytes for (device, stream); grows it with
+// stream-ordered allocation so the old buffer is released after queued work.
+int get_workspace(int device, cudaStream_t s, size_t need, void** out) {
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  Workspace& ws = g_ws[{device, s}];
+  if (ws.bytes < need) {
+    if (ws.ptr) {
+      cudaError_t e = cudaFreeAsync(ws.ptr, s);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync(workspace)");
+      ws.ptr = nullptr;
+      ws.bytes = 0;
+    }
+    const size_t bytes = align_up(need, 1 << 20);
+    cudaError_t e = cudaMallocAsync(&ws.ptr, bytes, s);
+    if (e != cudaSuccess) {
+      ws.ptr = nullptr;
+      return cuda_fail(e, "cudaMallocAsync(workspace)");
+    }
+    ws.bytes = bytes;
+  }
+  *out = ws.ptr;
+  return Q8LIN_OK;
+}
+
+int validate_weight(const q8lin_weight* w) {
+  if (!w) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "weight handle is null");
+  if (!w->packed || w->n <= 0 || w->k <= 0) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "weight handle is not initialised");
+  return Q8LIN_OK;
+}
+
+}  // namespace
+}  // namespace q8lin
+
+using namespace q8lin;
+
+extern "C" {
+
+int q8lin_version(void) { return Q8LIN_VERSION; }
+
+const char* q8lin_last_error(void) { return g_last_error.c_str(); }
+
+const char* q8lin_status_string(int status) {
+  switch (status) {
+    case Q8LIN_OK: return "Q8LIN_OK";
+    case Q8LIN_ERR_INVALID_ARGUMENT: return "Q8LIN_ERR_INVALID_ARGUMENT";
+    case Q8LIN_ERR_SHAPE: return "Q8LIN_ERR_SHAPE";
+    case Q8LIN_ERR_ALIGNMENT: return "Q8LIN_ERR_ALIGNMENT";
+    case Q8LIN_ERR_CUDA: return "Q8LIN_ERR_CUDA";
+    case Q8LIN_ERR_NCCL: return "Q8LIN_ERR_NCCL";
+    case Q8LIN_ERR_OUT_OF_MEMORY: return "Q8LIN_ERR_OUT_OF_MEMORY";
+    case Q8LIN_ERR_DEVICE: return "Q8LIN_ERR_DEVICE";
+    case Q8LIN_ERR_WORKSPACE: return "Q8LIN_ERR_WORKSPACE";
+    default: return "Q8LIN_ERR_UNKNOWN";
+  }
+}
+
+int q8lin_weight_create(const void* gguf_blocks, int64_t n, int64_t k, int device,
+                        q8lin_stream_t stream, q8lin_weight** out) {
+  if (!out) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "out is null");
+  *out = nullptr;
+  if (!gguf_blocks) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "gguf_blocks is null");
+  if (n <= 0 || k <= 0) return fail(Q8LIN_ERR_SHAPE, "weight shape must be positive, got (" + std::to_string(n) + ", " + std::to_string(k) + ")");
+  if (k % kQK) return fail(Q8LIN_ERR_SHAPE, "in-features " + std::to_string(k) + " is not a multiple of the Q8_0 block size 32");
+  if (n > (int64_t)1 << 30 || k > (int64_t)1 << 24)
+    return fail(Q8LIN_ERR_SHAPE, "weight shape beyond supported limits (n <= 2^30, k <= 2^24)");
+  int st = check_device(device);
+  if (st != Q8LIN_OK) return st;
+  DeviceGuard guard(device);
+  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+  const int64_t nb = k / kQK;
+  const size_t src_bytes = (size_t)(n * nb * kBlockBytes);
+  cudaPointerAttributes attr = {};
+  cudaError_t e = cudaPointerGetAttributes(&attr, gguf_blocks);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    attr.type = cudaMemoryTypeUnregistered;
+  }
+  const bool on_device = (attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged);
+  if (on_device && attr.type == cudaMemoryTypeDevice && attr.device != device)
+    return fail(Q8LIN_ERR_DEVICE, "gguf_blocks live on device " + std::to_string(attr.device) + ", not " + std::to_string(device));
+  if (on_device && (reinterpret_cast<uintptr_t>(gguf_blocks) & 1u))
+    return fail(Q8LIN_ERR_ALIGNMENT, "device gguf_blocks must be 2-byte aligned");
+
+  q8lin_weight* w = new q8lin_weight();
+  w->device = device;
+  w->n = n;
+  w->k = k;
+  w->row_stride = packed_row_stride(k);
+  w->bytes = (size_t)(n * w->row_stride);
+  e = cudaMalloc(&w->packed, w->bytes);
+  if (e != cudaSuccess) {
+    delete w;
+    return cuda_fail(e, "cudaMalloc(weight)");
+  }
+  const uint8_t* src = static_cast<const uint8_t*>(gguf_blocks);
+  uint8_t* staging = nullptr;
+  if (!on_device) {
+    e = cudaMalloc(&staging, src_bytes);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(staging, gguf_blocks, src_bytes, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) {
+      cudaFree(staging);
+      cudaFree(w->packed);
+      delete w;
+      return cuda_fail(e, "upload of gguf_blocks");
+    }
+    src = staging;
+  }
+  e = launch_repack(src, w->packed, n, k, w->row_stride, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (staging) cudaFree(staging);
+  if (e != cudaSuccess) {
+    cudaFree(w->packed);
+    delete w;
+    return cuda_fail(e, "repack");
+  }
+  *out = w;
+  return Q8LIN_OK;
+}
+
+int q8lin_weight_destroy(q8lin_weight* w) {
+  if (!w) return Q8LIN_OK;
+  DeviceGuard guard(w->device);
+  cudaError_t e = w->packed ? cudaFree(w->packed) : cudaSuccess;
+  delete w;
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree(weight)");
+  return Q8LIN_OK;
+}
+
+int q8lin_weight_shape(const q8lin_weight* w, int64_t* n, int64_t* k, int* device) {
+  int st = validate_weight(w);
+  if (st != Q8LIN_OK) return st;
+  if (n) *n = w->n;
+  if (k) *k = w->k;
+  if (device) *device = w->device;
+  return Q8LIN_OK;
+}
+
+int q8lin_weight_device_bytes(const q8lin_weight* w, size_t* bytes) {
+  int st = validate_weight(w);
+  if (st != Q8LIN_OK) return st;
+  if (!bytes) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "bytes is null");
+  *bytes = w->bytes;
+  return Q8LIN_OK;
+}
+
+int q8lin_weight_dequantize(const q8lin_weight* w, float* out, q8lin_stream_t stream) {
+  int st = validate_weight(w);
+  if (st != Q8LIN_OK) return st;
+  if (!out) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "out is null");
+  if (!aligned16(out)) return fail(Q8LIN_ERR_ALIGNMENT, "out must be 16-byte aligned");
+  DeviceGuard guard(w->device);
+  cudaError_t e = launch_dequantize(w->packed, out, w->n, w->k, w->row_stride, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "dequantize launch");
+  return Q8LIN_OK;
+}
+
+int q8lin_weight_export_gguf(const q8lin_weight* w, void* out_blocks, q8lin_stream_t stream) {
+  int st = validate_weight(w);
+  if (st != Q8LIN_OK) return st;
+  if (!out_blocks) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "out_blocks is null");
+  if (reinterpret_cast<uintptr_t>(out_blocks) & 1u) return fail(Q8LIN_ERR_ALIGNMENT, "out_blocks must be 2-byte aligned");
+  DeviceGuard guard(w->device);
+  cudaError_t e = launch_unpack(w->packed, static_cast<uint8_t*>(out_blocks), w->n, w->k, w->row_stride,
+                                reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "export launch");
+  return Q8LIN_OK;
+}
+
+size_t q8lin_workspace_size(const q8lin_weight* w, int64_t m) {
+  if (!w || m <= 0) return 0;
+  return workspace_bytes(m, w->k);
+}
+
+int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m, void* workspace,
+                     size_t workspace_bytes_avail, q8lin_stream_t stream) {
+  int st = validate_weight(w);
+  if (st != Q8LIN_OK) return st;
+  if (m < 0) return fail(Q8LIN_ERR_SHAPE, "row count must be non-negative, got " + std::to_string(m));
+  if (m == 0) return Q8LIN_OK;
+  if (m > (int64_t)1 << 24) return fail(Q8LIN_ERR_SHAPE, "row count beyond supported limit 2^24");
+  if (!x || !y) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "x and y must be non-null device pointers");
+  if (!aligned16(x) || !aligned16(y)) return fail(Q8LIN_ERR_ALIGNMENT, "x and y must be 16-byte aligned");
+  DeviceGuard guard(w->device);
+  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (use_gemv(m, w->k)) {
+    e = launch_gemv(*w, x, y, (int)m, s);
+    if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+    return Q8LIN_OK;
+  }
+  const size_t need = workspace_bytes(m, w->k);
+  if (!workspace || workspace_bytes_avail < need)
+    return fail(Q8LIN_ERR_WORKSPACE, "workspace of " + std::to_string(workspace_bytes_avail) + " bytes is smaller than the " +
+                                         std::to_string(need) + " bytes needed for M=" + std::to_string(m));
+  if (reinterpret_cast<uintptr_t>(workspace) % kAlign)
+    return fail(Q8LIN_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  int8_t* qx = static_cast<int8_t*>(workspace);
+  float* dx = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align_up((size_t)(m * w->k), kAlign));
+  e = launch_quantize_rows(x, m, w->k, qx, nullptr, dx, s);
+  if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+  e = launch_gemm(*w, qx, dx, y, m, s);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  return Q8LIN_OK;
+}
+
+int q8lin_forward(const q8lin_weight* w, const float* x, float* y, int64_t m, q8lin_stream_t stream) {
+  int st = validate_weight(w);
+  if (st != Q8LIN_OK) return st;
+  if (m <= 0 || use_gemv(m, w->k)) return q8lin_forward_ws(w, x, y, m, nullptr, 0, stream);
+  DeviceGuard guard(w->device);
+  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
+  void* ws = nullptr;
+  const size_t need = workspace_bytes(m, w->k);
+  st = get_workspace(w->device, reinterpret_cast<cudaStream_t>(stream), need, &ws);
+  if (st != Q8LIN_OK) return st;
+  return q8lin_forward_ws(w, x, y, m, ws, need, stream);
+}
+
+int q8lin_reserve_workspace(int device, q8lin_stream_t stream, int64_t m, int64_t k) {
+  if (m < 0 || k <= 0 || k % kQK) return fail(Q8LIN_ERR_SHAPE, "reserve needs m >= 0 and k a positive multiple of 32");
+  int st = check_device(device);
+  if (st != Q8LIN_OK) return st;
+  const size_t need = workspace_bytes(m, k);
+  if (need == 0) return Q8LIN_OK;
+  DeviceGuard guard(device);
+  void* ws = nullptr;
+  return get_workspace(device, reinterpret_cast<cudaStream_t>(stream), need, &ws);
+}
+
+int q8lin_quantize_rows(const float* x, int64_t m, int64_t k, int8_t* qs, uint16_t* d_f16,
+                        q8lin_stream_t stream) {
+  if (m < 0 || k <= 0 || k % kQK) return fail(Q8LIN_ERR_SHAPE, "quantize needs m >= 0 and k a positive multiple of 32");
+  if (m == 0) return Q8LIN_OK;
+  if (!x || !qs || !d_f16) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "x, qs and d_f16 must be non-null device pointers");
+  if (!aligned16(x) || !aligned16(qs) || (reinterpret_cast<uintptr_t>(d_f16) & 1u))
+    return fail(Q8LIN_ERR_ALIGNMENT, "x and qs must be 16-byte aligned, d_f16 2-byte aligned");
+  cudaError_t e = launch_quantize_rows(x, m, k, qs, d_f16, nullptr, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+  return Q8LIN_OK;
+}
+
+}  // extern "C"

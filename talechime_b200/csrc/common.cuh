@@ -1,0 +1,109 @@
+// Device helpers shared by the Q8_0 kernels (sm_100a only).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "talechime_b200 kernels target sm_100a only"
+#endif
+
+namespace q8lin {
+
+constexpr int kQK = 32;          // values per Q8_0 block
+constexpr int kBlockBytes = 34;  // GGUF block bytes
+constexpr unsigned kFull = 0xffffffffu;
+
+// Bytes of one repacked weight row: K int8 values, K/32 f16 scales, padded to 16 B.
+__host__ __device__ inline int64_t packed_row_stride(int64_t k) {
+  return k + (((k / 16) + 15) / 16) * 16;
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  No-ops unless the launch set the attribute.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Streaming loads (read-only, no L1 allocation).
+__device__ __forceinline__ int4 ld_stream_v4(const void* p) {
+  int4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+__device__ __forceinline__ int dot16(const int4 a, const int4 b, int c) {
+  c = __dp4a(a.x, b.x, c);
+  c = __dp4a(a.y, b.y, c);
+  c = __dp4a(a.z, b.z, c);
+  c = __dp4a(a.w, b.w, c);
+  return c;
+}
+
+// ---------------------------------------------------------------------------
+// Candle's Q8_0 quantization of one value (BlockQ8_0::from_float):
+// q = (i8) round_half_away(v * id), saturating, NaN -> 0.
+__device__ __forceinline__ int quant_q8(float v, float id) {
+  const float p = __fmul_rn(v, id);     // one rounding, never fused
+  const float r = roundf(p);            // half away from zero
+  int q = __float2int_rz(r);            // saturates; NaN -> 0
+  q = max(-128, min(127, q));
+  return q;
+}
+
+// Per-block quantization parameters: d = amax/127 (IEEE division),
+// id = d != 0 ? 1/d : 0, d_f16 = RNE(d).
+struct QParams {
+  float id;
+  __half d_h;
+};
+__device__ __forceinline__ QParams block_qparams(float amax) {
+  QParams p;
+  const float d = __fdiv_rn(amax, 127.0f);
+  p.id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+  p.d_h = __float2half_rn(d);
+  return p;
+}
+
+// f32 max that skips NaN (Rust f32::max / C fmaxf semantics).
+__device__ __forceinline__ float nan_skip_max(float a, float b) { return fmaxf(a, b); }
+
+// Quantize one 32-value block held as 8 float4 in registers into 8 packed int32.
+__device__ __forceinline__ void quantize_block_regs(const float4 (&v)[8], int (&q)[8],
+                                                    __half& d_h) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    amax = nan_skip_max(amax, fabsf(v[t].x));
+    amax = nan_skip_max(amax, fabsf(v[t].y));
+    amax = nan_skip_max(amax, fabsf(v[t].z));
+    amax = nan_skip_max(amax, fabsf(v[t].w));
+  }
+  const QParams p = block_qparams(amax);
+  d_h = p.d_h;
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    const int a = quant_q8(v[t].x, p.id);
+    const int b = quant_q8(v[t].y, p.id);
+    const int c = quant_q8(v[t].z, p.id);
+    const int d = quant_q8(v[t].w, p.id);
+    q[t] = (a & 0xff) | ((b & 0xff) << 8) | ((c & 0xff) << 16) | ((d & 0xff) << 24);
+  }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+}  // namespace q8lin

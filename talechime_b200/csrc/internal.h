@@ -1,0 +1,46 @@
+// Host-side declarations shared by the translation units of libq8lin.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+struct q8lin_weight {
+  int device = -1;
+  int64_t n = 0;           // out features (rows)
+  int64_t k = 0;           // in features
+  int64_t row_stride = 0;  // bytes per repacked row
+  uint8_t* packed = nullptr;
+  size_t bytes = 0;
+};
+
+namespace q8lin {
+
+// Error plumbing (thread-local message).
+int fail(int status, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+// Kernel launchers (return cudaError_t of the launch).
+cudaError_t launch_repack(const uint8_t* gguf, uint8_t* packed, int64_t n, int64_t k,
+                          int64_t row_stride, cudaStream_t s);
+cudaError_t launch_unpack(const uint8_t* packed, uint8_t* gguf, int64_t n, int64_t k,
+                          int64_t row_stride, cudaStream_t s);
+cudaError_t launch_dequantize(const uint8_t* packed, float* out, int64_t n, int64_t k,
+                              int64_t row_stride, cudaStream_t s);
+cudaError_t launch_quantize_rows(const float* x, int64_t m, int64_t k, int8_t* qs,
+                                 uint16_t* d_f16, float* d_f32, cudaStream_t s);
+
+// Decode GEMV for 1 <= m <= kGemvMaxM.
+constexpr int kGemvMaxM = 16;
+cudaError_t launch_gemv(const q8lin_weight& w, const float* x, float* y, int m,
+                        cudaStream_t s);
+
+// Batched path for m > kGemvMaxM over pre-quantized activations.
+cudaError_t launch_gemm(const q8lin_weight& w, const int8_t* qx, const float* dx, float* y,
+                        int64_t m, cudaStream_t s);
+
+int sm_count(int device);
+
+}  // namespace q8lin

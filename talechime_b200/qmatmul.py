@@ -1,0 +1,190 @@
+"""Host-side mirror of the operator surface talechime calls for Q8_0 projections.
+
+* ``QMatMul`` -- candle's ``QMatMul::QTensor(Arc<QTensor>)`` for ``GgmlDType::Q8_0``
+  as built at crates/voxcpm/src/weights.rs:103-104: holds one GGUF Q8_0 tensor on a
+  B200 and computes ``forward(x[M, K]) -> y[M, N]``.
+* ``Linear`` -- ``voxcpm::weights::Linear`` (crates/voxcpm/src/weights.rs:209-229):
+  flattens x to ``[rows, in]``, calls ``QMatMul.forward`` and adds an optional bias.
+
+All arithmetic runs in libq8lin.so (hand-written sm_100a kernels); this module only
+checks arguments the way candle does, allocates outputs and passes pointers.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import Q8LinError, check
+
+QK8_0 = 32
+BLOCK_BYTES = 34
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class QMatMul:
+    """One Q8_0 projection resident on one GPU (candle shape ``(n, k)`` = (out, in))."""
+
+    def __init__(self, handle: ctypes.c_void_p, n: int, k: int, device: torch.device):
+        self._handle = handle
+        self.n = n
+        self.k = k
+        self.device = device
+
+    # -- construction --------------------------------------------------------------
+    @classmethod
+    def from_gguf_blocks(cls, blocks, n: int, k: int,
+                         device: Optional[torch.device | int | str] = None) -> "QMatMul":
+        """Upload N rows of K/32 GGUF Q8_0 blocks (34 bytes each).
+
+        ``blocks`` may be ``bytes``, a uint8 numpy array, or a uint8 torch tensor on
+        the CPU or on the target GPU.  Mirrors ``Content::tensor`` + ``QTensor``
+        construction (crates/voxcpm/src/weights.rs:100-104).
+        """
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise ValueError("QMatMul lives on a CUDA device; there is no CPU path")
+        if k <= 0 or k % QK8_0:
+            raise Q8LinError(_lib.ERR_SHAPE, f"in-features {k} is not a multiple of 32")
+        nbytes = n * (k // QK8_0) * BLOCK_BYTES
+        keep = None
+        if isinstance(blocks, (bytes, bytearray, memoryview)):
+            arr = np.frombuffer(blocks, dtype=np.uint8)
+            keep = arr
+            ptr = arr.ctypes.data
+            size = arr.size
+        elif isinstance(blocks, np.ndarray):
+            arr = np.ascontiguousarray(blocks.view(np.uint8) if blocks.dtype != np.uint8 else blocks)
+            keep = arr
+            ptr = arr.ctypes.data
+            size = arr.size
+        elif isinstance(blocks, torch.Tensor):
+            t = blocks.contiguous()
+            if t.dtype != torch.uint8:
+                raise TypeError("GGUF blocks must be a uint8 tensor")
+            if t.is_cuda and t.device != device:
+                raise ValueError(f"blocks are on {t.device}, weight requested on {device}")
+            keep = t
+            ptr = t.data_ptr()
+            size = t.numel()
+        else:
+            raise TypeError(f"unsupported block container {type(blocks)!r}")
+        if size != nbytes:
+            raise Q8LinError(_lib.ERR_SHAPE,
+                             f"{size} bytes of blocks do not match ({n}, {k}) Q8_0 = {nbytes} bytes")
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            check(_lib.lib().q8lin_weight_create(ctypes.c_void_p(ptr), n, k, device.index,
+                                                 ctypes.c_void_p(_stream_ptr(device)),
+                                                 ctypes.byref(handle)))
+        del keep
+        return cls(handle, n, k, device)
+
+    def __del__(self):
+        h = getattr(self, "_handle", None)
+        if h is not None and h.value:
+            try:
+                _lib.lib().q8lin_weight_destroy(h)
+            except Exception:
+                pass
+            self._handle = None
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._handle
+
+    def shape(self) -> tuple[int, int]:
+        return (self.n, self.k)
+
+    def device_bytes(self) -> int:
+        out = ctypes.c_size_t()
+        check(_lib.lib().q8lin_weight_device_bytes(self._handle, ctypes.byref(out)))
+        return out.value
+
+    # -- compute -------------------------------------------------------------------
+    def _check_input(self, x: torch.Tensor) -> None:
+        # candle QTensor::cpu_fwd / cuda_fwd rules for the quantized matmul
+        if x.dim() < 2:
+            raise Q8LinError(_lib.ERR_SHAPE, f"input tensor has only one dimension {tuple(x.shape)}")
+        if x.shape[-1] != self.k:
+            raise Q8LinError(_lib.ERR_SHAPE,
+                             f"input tensor {tuple(x.shape)} incompatible with ({self.n}, {self.k})")
+        if x.dtype != torch.float32:
+            raise Q8LinError(_lib.ERR_INVALID_ARGUMENT, f"input dtype {x.dtype} is not f32")
+        if not x.is_contiguous():
+            raise Q8LinError(_lib.ERR_INVALID_ARGUMENT, "input tensor is not contiguous")
+        if x.device != self.device:
+            raise Q8LinError(_lib.ERR_DEVICE, f"input on {x.device}, weight on {self.device}")
+
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y[..., N] = x[..., K] . W^T with candle's Q8_0 CPU semantics (QMatMul::forward)."""
+        self._check_input(x)
+        m = x.numel() // self.k
+        if out is None:
+            out = torch.empty(x.shape[:-1] + (self.n,), dtype=torch.float32, device=self.device)
+        elif out.shape != x.shape[:-1] + (self.n,) or out.dtype != torch.float32 or not out.is_contiguous():
+            raise Q8LinError(_lib.ERR_SHAPE, "out has the wrong shape, dtype or layout")
+        check(_lib.lib().q8lin_forward(self._handle, ctypes.c_void_p(x.data_ptr()),
+                                       ctypes.c_void_p(out.data_ptr()), m,
+                                       ctypes.c_void_p(_stream_ptr(self.device))))
+        return out
+
+    __call__ = forward
+
+    def dequantize(self) -> torch.Tensor:
+        """f32 [N, K] (QTensor::dequantize, crates/voxcpm/src/weights.rs:79-80,106)."""
+        out = torch.empty((self.n, self.k), dtype=torch.float32, device=self.device)
+        check(_lib.lib().q8lin_weight_dequantize(self._handle, ctypes.c_void_p(out.data_ptr()),
+                                                 ctypes.c_void_p(_stream_ptr(self.device))))
+        return out
+
+    def to_gguf_blocks(self) -> torch.Tensor:
+        """The weight in GGUF block layout, uint8 [N, K/32, 34] on the device."""
+        out = torch.empty((self.n, self.k // QK8_0, BLOCK_BYTES), dtype=torch.uint8, device=self.device)
+        check(_lib.lib().q8lin_weight_export_gguf(self._handle, ctypes.c_void_p(out.data_ptr()),
+                                                  ctypes.c_void_p(_stream_ptr(self.device))))
+        return out
+
+
+class Linear:
+    """voxcpm ``Linear { mat: QMatMul, bias: Option<Tensor> }`` (weights.rs:209-229)."""
+
+    def __init__(self, mat: QMatMul, bias: Optional[torch.Tensor] = None):
+        self.mat = mat
+        self.bias = bias
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.dim() == 0:
+            raise Q8LinError(_lib.ERR_SHAPE, "linear input must have dimensions")
+        shape = list(x.shape)
+        inp = shape[-1]
+        rows = x.numel() // inp if inp else 0
+        y = self.mat.forward(x.contiguous().reshape(rows, inp))
+        shape[-1] = y.shape[1]
+        y = y.reshape(shape)
+        if self.bias is not None:
+            y = y + self.bias
+        return y
+
+    __call__ = forward
+
+
+def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Device Q8_0 quantization of f32 rows: (qs int8 [M, K], d f16 [M, K/32])."""
+    if x.dim() != 2 or x.dtype != torch.float32 or not x.is_cuda or not x.is_contiguous():
+        raise Q8LinError(_lib.ERR_INVALID_ARGUMENT, "quantize_rows needs a contiguous f32 [M, K] CUDA tensor")
+    m, k = x.shape
+    qs = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    d = torch.empty((m, k // QK8_0), dtype=torch.float16, device=x.device)
+    check(_lib.lib().q8lin_quantize_rows(ctypes.c_void_p(x.data_ptr()), m, k,
+                                         ctypes.c_void_p(qs.data_ptr()), ctypes.c_void_p(d.data_ptr()),
+                                         ctypes.c_void_p(_stream_ptr(x.device))))
+    return qs, d
