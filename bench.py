@@ -252,7 +252,9 @@ def main() -> None:
     torch.cuda.synchronize()
     xs = {k: torch.randn((1, k), generator=gen, device=dev) for _, k, _ in SHAPES}
     ys = [torch.empty((1, m.n), device=dev) for m in mats]
-    stream = torch.cuda.current_stream(dev)
+    # all timed work runs on one non-default stream (graph capture needs one)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
     sptr = ctypes.c_void_p(stream.cuda_stream)
     handles = [m.handle for m in mats]
     xptr = [ctypes.c_void_p(xs[m.k].data_ptr()) for m in mats]

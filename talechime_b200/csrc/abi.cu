@@ -1,6 +1,7 @@
 // C ABI of libq8lin.so (declared in include/q8lin.h): argument checks, weight
 // upload/repack, workspace management and dispatch to the kernels.
 #include <cuda_runtime.h>
+#include <stdlib.h>
 
 #include <map>
 #include <mutex>
@@ -36,7 +37,13 @@ int sm_count(int device) {
   return cache[device];
 }
 
-size_t gemv_smem_bytes(int m, int64_t k);  // gemv.cu
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("Q8LIN_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 namespace {
 

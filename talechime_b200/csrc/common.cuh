@@ -39,6 +39,11 @@ __device__ __forceinline__ int4 ld_stream_v4(const void* p) {
   return v;
 }
 
+// Bulk prefetch of [p, p + bytes) into L2 (p and bytes multiples of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
 __device__ __forceinline__ int dot16(const int4 a, const int4 b, int c) {
@@ -98,6 +103,25 @@ __device__ __forceinline__ void quantize_block_regs(const float4 (&v)[8], int (&
     const int d = quant_q8(v[t].w, p.id);
     q[t] = (a & 0xff) | ((b & 0xff) << 8) | ((c & 0xff) << 16) | ((d & 0xff) << 24);
   }
+}
+
+// Octet-parallel quantization: the 32 values of one block are held by 8 consecutive
+// lanes (lane & ~7 aligned), 4 values each.  Every lane of the warp must call this
+// (the amax is combined with shuffles).  Returns the lane's 4 int8 packed in an int;
+// d_h is the block's f16 scale (identical in the 8 lanes).
+__device__ __forceinline__ int quantize_octet(const float4 v, __half& d_h) {
+  float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+  amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 2));
+  amax = fmaxf(amax, __shfl_xor_sync(kFull, amax, 4));
+  amax = fmaxf(amax, 0.0f);  // all-NaN block: candle's running max starts at 0
+  const QParams p = block_qparams(amax);
+  d_h = p.d_h;
+  const int a = quant_q8(v.x, p.id);
+  const int b = quant_q8(v.y, p.id);
+  const int c = quant_q8(v.z, p.id);
+  const int d = quant_q8(v.w, p.id);
+  return (a & 0xff) | ((b & 0xff) << 8) | ((c & 0xff) << 16) | ((d & 0xff) << 24);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

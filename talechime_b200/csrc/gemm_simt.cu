@@ -98,7 +98,7 @@ cudaError_t launch_gemm(const q8lin_weight& w, const int8_t* qx, const float* dx
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, gemm_q8_0_simt_kernel, (const uint8_t*)w.packed, w.row_stride,
                             N, K, qx, dx, y, (int)m);
 }

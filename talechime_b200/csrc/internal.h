@@ -34,6 +34,7 @@ cudaError_t launch_quantize_rows(const float* x, int64_t m, int64_t k, int8_t* q
 
 // Decode GEMV for 1 <= m <= kGemvMaxM.
 constexpr int kGemvMaxM = 16;
+size_t gemv_smem_bytes(int m, int64_t k);
 cudaError_t launch_gemv(const q8lin_weight& w, const float* x, float* y, int m,
                         cudaStream_t s);
 
@@ -42,5 +43,8 @@ cudaError_t launch_gemm(const q8lin_weight& w, const int8_t* qx, const float* dx
                         int64_t m, cudaStream_t s);
 
 int sm_count(int device);
+
+// Programmatic dependent launch on/off (env Q8LIN_PDL=0 turns it off; read once).
+bool pdl_enabled();
 
 }  // namespace q8lin

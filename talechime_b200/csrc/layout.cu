@@ -143,7 +143,7 @@ cudaError_t launch_quantize_rows(const float* x, int64_t m, int64_t k, int8_t* q
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, quantize_rows_kernel, x, m, k, qs, d_f16, d_f32);
 }
 
