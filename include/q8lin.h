@@ -102,6 +102,22 @@ int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
 int q8lin_reserve_workspace(int device, q8lin_stream_t stream, int64_t m, int64_t k);
 
 /*
+ * No counterpart in the reference.  The same y = x . W^T for callers that must not
+ * allocate device memory during a call -- a real-time audio producer cannot stall
+ * on cudaMalloc's device synchronisation, and an embedder whose allocator owns all
+ * device memory may not be allowed to allocate around it.  The activation scratch
+ * is a fixed device array inside the library (9 MiB per GPU that loads it, held
+ * until exit), so this call allocates nothing.  Limit: M*K <= Q8LIN_NOALLOC_MAX_VALUES;
+ * larger inputs return Q8LIN_ERR_SHAPE.  The first call on a device looks up the
+ * array's device address, so make it before any stream capture.  All calls on a
+ * device share the array: calls that overlap on the GPU race (calls issued on one
+ * stream are ordered).
+ */
+#define Q8LIN_NOALLOC_MAX_VALUES 8388608
+int q8lin_forward_noalloc(const q8lin_weight* w, const float* x, float* y, int64_t m,
+                          q8lin_stream_t stream);
+
+/*
  * Quantize f32 activations x[M][K] to Q8_0 planes on the device: qs int8 [M][K]
  * and d as f16 bits [M][K/32].  The quantizer every forward path uses (candle's
  * BlockQ8_0::from_float applied to the lhs rows of its CPU matmul).
