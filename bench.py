@@ -195,7 +195,84 @@ def config_block(world: int) -> dict:
             "parallelism": f"replicas x{world}"}
 
 
-# --------------------------------------------------------------------------- GPU leg
+# --------------------------------------------------------------------------- GPU legs
+def _device_weight(torch, gen, dev, n, k):
+    """Random Q8_0 GGUF blocks generated on the device, uploaded through the C ABI."""
+    from talechime_b200 import QMatMul
+
+    nb = k // 32
+    blocks = torch.empty((n, nb, 34), dtype=torch.uint8, device=dev)
+    qs = torch.randint(-127, 128, (n, nb, 32), generator=gen, device=dev, dtype=torch.int8)
+    d = (torch.randn((n, nb), generator=gen, device=dev).abs() * (0.02 / 127.0)).half()
+    blocks[:, :, 2:] = qs.view(torch.uint8)
+    blocks[:, :, :2] = d.view(torch.uint8).view(n, nb, 2)
+    return QMatMul.from_gguf_blocks(blocks, n, k, device=dev)
+
+
+def time_shape(torch, L, dev, stream, gen, m, k, n, reps, copies=3):
+    """Device time of q8lin_forward_ws for one shape, rotating `copies` weight copies."""
+    mats = [_device_weight(torch, gen, dev, n, k) for _ in range(copies)]
+    x = torch.randn((m, k), generator=gen, device=dev)
+    y = torch.empty((m, n), device=dev)
+    need = L.q8lin_workspace_size(mats[0].handle, m)
+    ws = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+
+    def run(i):
+        st = L.q8lin_forward_ws(mats[i % copies].handle, ctypes.c_void_p(x.data_ptr()),
+                                ctypes.c_void_p(y.data_ptr()), m, ctypes.c_void_p(ws.data_ptr()), need, sptr)
+        if st:
+            from talechime_b200 import _lib
+            _lib.check(st)
+
+    for i in range(3):
+        run(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(reps):
+        run(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del mats
+    return ms
+
+
+def run_case(args) -> None:
+    import torch
+
+    from talechime_b200 import _lib, build
+
+    m, k, n = (int(v) for v in args.case.split(":"))
+    build.build()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    ms = time_shape(torch, _lib.lib(), dev, stream, gen, m, k, n, max(args.steps, 1))
+    ops = 2.0 * m * n * k
+    byts = algorithmic_bytes(m, k, n)
+    print(json.dumps({"case": {"m": m, "k": k, "n": n}, "us": ms * 1e3, "tflops": ops / ms / 1e9,
+                      "gbs": byts / ms / 1e6, "note": "profiling case; not a bench line"}), flush=True)
+
+
+def run_sweep(torch, L, dev, stream) -> list:
+    """M in {1,4,16,64,256,1024} x the four projection shapes."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+    out = []
+    for name, k, n in SHAPES:
+        for m in (1, 4, 16, 64, 256, 1024):
+            ms = time_shape(torch, L, dev, stream, gen, m, k, n, 20)
+            out.append({"shape": name, "m": m, "k": k, "n": n, "us": round(ms * 1e3, 2),
+                        "tb_s": round(algorithmic_bytes(m, k, n) / ms / 1e9, 3),
+                        "tflop_s": round(2.0 * m * n * k / ms / 1e9, 1)})
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -207,6 +284,10 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layer copies (28 = the benchmark; fewer only for small profiling captures)")
+    ap.add_argument("--case", default=None,
+                    help="M:K:N -- run one projection shape `--steps` times (profiling), print its timing")
+    ap.add_argument("--sweep", action="store_true",
+                    help="also time the BASELINE configs[1] shape sweep (M x {qkv,o,gate_up,down}) into the line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -220,6 +301,10 @@ def main() -> None:
 
     import torch
     import torch.distributed as dist
+
+    if args.case:
+        run_case(args)
+        return
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -382,6 +467,8 @@ def main() -> None:
             "value": v, "unit": "TB/s", "cores": threads, "kind": "port",
             "sample": f"{done} projections (qkv/o/gate_up/down of 2 layers, M=1) in {el:.1f} s with the "
                       f"candle-CPU restatement (oracle/q8_0_oracle.c)"}
+    if args.sweep and rank == 0:
+        line["sweep"] = run_sweep(torch, L, dev, stream)
     if rank == 0:
         print(json.dumps(line), flush=True)
     del graph

@@ -81,7 +81,8 @@ int q8lin_weight_dequantize(const q8lin_weight* w, float* out, q8lin_stream_t st
 /* Write the weight back in GGUF block layout (device memory, N*K/32*34 bytes). */
 int q8lin_weight_export_gguf(const q8lin_weight* w, void* out_blocks, q8lin_stream_t stream);
 
-/* Workspace bytes q8lin_forward_ws needs for M rows (0 for M <= 16). */
+/* Workspace bytes q8lin_forward_ws needs for M rows (0 for M <= 16): the activations as
+ * f16 integers [M][K] plus transposed f32 scales [K/32][M], each 256-byte aligned. */
 size_t q8lin_workspace_size(const q8lin_weight* w, int64_t m);
 
 /*
@@ -116,6 +117,14 @@ int q8lin_reserve_workspace(int device, q8lin_stream_t stream, int64_t m, int64_
 #define Q8LIN_NOALLOC_MAX_VALUES 8388608
 int q8lin_forward_noalloc(const q8lin_weight* w, const float* x, float* y, int64_t m,
                           q8lin_stream_t stream);
+
+/*
+ * Device-side fault word of `device` (bit 0: a tensor-core kernel's bounded wait ran
+ * out and the kernel returned early; its output is then invalid).  Reads it with a
+ * device synchronisation; `clear` resets it.  No counterpart in the reference (candle's
+ * kernels have no bounded waits); this is the library's failure-detection hook.
+ */
+int q8lin_fault_status(int device, uint32_t* flags, int clear);
 
 /*
  * Quantize f32 activations x[M][K] to Q8_0 planes on the device: qs int8 [M][K]

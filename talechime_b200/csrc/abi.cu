@@ -58,7 +58,7 @@ bool use_gemv(int64_t m, int64_t k) {
 
 size_t workspace_bytes(int64_t m, int64_t k) {
   if (m <= 0 || use_gemv(m, k)) return 0;
-  return align_up((size_t)(m * k), kAlign) + align_up((size_t)m * (size_t)(k / kQK) * sizeof(float), kAlign);
+  return gemm_tc_workspace_bytes(m, k);
 }
 
 // Makes `device` current for the scope and restores the caller's device.
@@ -304,12 +304,8 @@ int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
                                          std::to_string(need) + " bytes needed for M=" + std::to_string(m));
   if (reinterpret_cast<uintptr_t>(workspace) % kAlign)
     return fail(Q8LIN_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
-  int8_t* qx = static_cast<int8_t*>(workspace);
-  float* dx = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align_up((size_t)(m * w->k), kAlign));
-  e = launch_quantize_rows(x, m, w->k, qx, nullptr, dx, s);
-  if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
-  e = launch_gemm(*w, qx, dx, y, m, s);
-  if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  e = launch_gemm_tc(*w, x, workspace, y, m, s);
+  if (e != cudaSuccess) return cuda_fail(e, "tensor-core gemm launch");
   return Q8LIN_OK;
 }
 
@@ -335,6 +331,18 @@ int q8lin_reserve_workspace(int device, q8lin_stream_t stream, int64_t m, int64_
   DeviceGuard guard(device);
   void* ws = nullptr;
   return get_workspace(device, reinterpret_cast<cudaStream_t>(stream), need, &ws);
+}
+
+int q8lin_fault_status(int device, uint32_t* flags, int clear) {
+  if (!flags) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "flags is null");
+  int st = check_device(device);
+  if (st != Q8LIN_OK) return st;
+  DeviceGuard guard(device);
+  unsigned int f = 0;
+  cudaError_t e = read_tc_fault(&f, clear != 0);
+  if (e != cudaSuccess) return cuda_fail(e, "read fault word");
+  *flags = f;
+  return Q8LIN_OK;
 }
 
 int q8lin_quantize_rows(const float* x, int64_t m, int64_t k, int8_t* qs, uint16_t* d_f16,

@@ -1,0 +1,550 @@
+// Batched Q8_0 matmul on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// y[m][n] = sum_b dw[n][b] * dx[m][b] * I[m][n][b],  I = exact int dot of one 32-value
+// block.  The per-block scales forbid accumulating across blocks inside the MMA, so
+// every 32-value block gets its own tensor-core product and the rescale happens in
+// registers:
+//   * A = activations (MMA M = 128 rows of x), f16 holding the exact Q8_0 integers
+//     (written by quantize_rows_f16t), 128B-swizzled tiles loaded by TMA;
+//   * B = weights (MMA N = 128 rows of W), int8 tiles loaded by TMA from the packed
+//     plane and widened to f16 integers in shared memory by converter warps (same
+//     swizzled K-major layout);
+//   * per block: two tcgen05.mma kind::f16 (K = 16 each) into a fresh TMEM buffer
+//     (f32; products of |q| <= 127 and their 32-term sums are exact integers);
+//   * epilogue warps read the block's 128x128 result with tcgen05.ld and accumulate
+//     acc += I * (dw * dx) in f32 registers (packed f32x2 math); TMEM holds two
+//     stages' worth of block results (4 x 128 columns), handed over a stage at a time,
+//     so the MMAs of stage s+1 run while stage s is rescaled.
+// One CTA owns a 128 (m) x 128 (n) output tile over the whole K.
+//
+// Three rings keep the loads far ahead of the math (a stage = 64 K values = 2 blocks):
+//   operand ring (kStages): A f16 tile + B int8 tile, freed by the MMA commit;
+//   f16 weight ring (2 slots): converted B, freed by the MMA commit;
+//   scale ring (kScSlots): activation scales (TMA) + weight scales (converters),
+//     freed by the epilogue.
+//
+// Warp roles (512 threads):
+//   warp 0      TMA producer (waits on the upstream kernel before loading activations)
+//   warp 1      TMEM allocation and MMA issue (one elected lane)
+//   warps 2-7   int8 -> f16 conversion of the weight tile, weight scales -> smem
+//   warps 8-15  epilogue: TMEM lane quadrant (warp % 4) x column half ((warp - 8) / 4)
+//
+// Every mbarrier wait is bounded; a wait that runs out sets a fault word that the host
+// reads with q8lin_fault_status and makes the CTA drain and return.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace q8lin {
+
+__device__ unsigned int g_tc_fault;  // bit 0: a bounded wait ran out
+
+namespace {
+
+constexpr int kBM = 128;          // activation rows per tile (MMA M)
+constexpr int kBN = 128;          // weight rows per tile (MMA N)
+constexpr int kBK = 64;           // K values per stage (two Q8_0 blocks)
+constexpr int kStages = 6;        // operand ring
+constexpr int kBSlots = 2;        // converted-weight ring
+constexpr int kScSlots = 8;       // scale ring
+constexpr int kThreads = 512;
+constexpr int kConvWarps = 6;     // warps 2..7
+constexpr int kConvThreads = kConvWarps * 32;
+constexpr int kEpiWarps = 8;
+constexpr int kAccBufs = 4;       // TMEM block buffers (4 x 128 columns = all of TMEM), used in pairs
+constexpr int kAccPairs = kAccBufs / 2;
+constexpr uint32_t kTmemCols = kAccBufs * kBN;
+constexpr uint32_t kSpinLimit = 1u << 24;
+
+constexpr int kAStageBytes = kBM * kBK * 2;   // 16 KB f16
+constexpr int kBStageBytes = kBN * kBK * 2;   // 16 KB f16
+constexpr int kB8StageBytes = kBN * kBK;      //  8 KB int8
+constexpr int kDxStageBytes = 2 * kBM * 4;    //  1 KB f32
+
+struct Smem {
+  alignas(1024) uint8_t a[kStages][kAStageBytes];
+  alignas(1024) uint8_t b[kBSlots][kBStageBytes];
+  alignas(128) uint8_t b8[kStages][kB8StageBytes];
+  alignas(128) float dx[kScSlots][2][kBM];  // activation scales of a stage's two blocks (TMA)
+  alignas(16) float dw[kScSlots][2][kBN];   // weight scales of a stage's two blocks
+  alignas(8) uint64_t full[kStages];        // A + B int8 landed
+  alignas(8) uint64_t empty[kStages];       // MMAs of the stage done (operands free)
+  alignas(8) uint64_t bfull[kBSlots];       // converted B written
+  alignas(8) uint64_t bempty[kBSlots];      // MMAs reading the converted B done
+  alignas(8) uint64_t dxfull[kScSlots];     // activation scales landed (TMA)
+  alignas(8) uint64_t dwfull[kScSlots];     // weight scales written (converter warps)
+  alignas(8) uint64_t scempty[kScSlots];    // epilogue done with the scales
+  alignas(8) uint64_t acc_full[kAccPairs];  // a stage's block results ready in a TMEM buffer pair
+  alignas(8) uint64_t acc_empty[kAccPairs]; // epilogue done reading the pair
+  alignas(8) uint64_t mma_done;             // every MMA this CTA issued has completed
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+// Bounded wait for the phase with the given parity; false (and the fault flag) on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
+  const uint32_t a = su32(b);
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+    if (ok) return true;
+    if ((i & 1023) == 1023 && *abort) return false;
+  }
+  *abort = 1;
+  atomicOr(&g_tc_fault, 1u);
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(su32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(su32(bar))
+      : "memory");
+}
+
+// K-major, 128B-swizzled UMMA shared-memory descriptor (8-row atoms of 128 B, SBO 1024 B).
+__device__ __forceinline__ uint64_t umma_desc_sw128(const void* base) {
+  const uint64_t addr = su32(base);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;           // start address
+  d |= (uint64_t)1 << 16;                 // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                 // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                 // layout: SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: kind::f16, A/B f16, D f32, both K-major, M = 128, N = kBN.
+constexpr uint32_t kIdesc = (1u << 4)                    // D format f32
+                          | (0u << 7) | (0u << 10)       // A, B f16
+                          | ((uint32_t)(kBN >> 3) << 17)  // N >> 3
+                          | ((uint32_t)(kBM >> 4) << 24); // M >> 4
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 lanes x 16 consecutive f32 columns of TMEM -> 16 registers per thread.  Issue only:
+// the values are valid after tcgen05.wait::ld.
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+  float2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
+  return d;
+}
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(reinterpret_cast<uint64_t&>(d))
+      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)),
+        "l"(reinterpret_cast<const uint64_t&>(c)));
+  return d;
+}
+
+// Four int8 -> four f16 holding the same integers: byte b becomes f16(1024 + (b ^ 0x80)),
+// then 1152 is subtracted (exact at this exponent).
+__device__ __forceinline__ uint2 i8x4_to_f16x4(uint32_t w) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t lo = __byte_perm(u, 0x64646464u, 0x5140);
+  const uint32_t hi = __byte_perm(u, 0x64646464u, 0x7362);
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+  const __half2 l = __hsub2(*reinterpret_cast<const __half2*>(&lo), bias);
+  const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&hi), bias);
+  uint2 r;
+  r.x = *reinterpret_cast<const uint32_t*>(&l);
+  r.y = *reinterpret_cast<const uint32_t*>(&h);
+  return r;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                    const __grid_constant__ CUtensorMap map_dx, const uint8_t* __restrict__ W, int64_t S, int N,
+                    int K, float* __restrict__ y, int M) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kBN;
+  const int m0 = blockIdx.y * kBM;
+  const int nb = K >> 5;
+  const int nstages = (K + kBK - 1) / kBK;
+  volatile int* abort = &sm.abort;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1);
+    }
+    for (int i = 0; i < kBSlots; ++i) {
+      mbar_init(&sm.bfull[i], kConvWarps);
+      mbar_init(&sm.bempty[i], 1);
+    }
+    for (int i = 0; i < kScSlots; ++i) {
+      mbar_init(&sm.dxfull[i], 1);
+      mbar_init(&sm.dwfull[i], kConvWarps);
+      mbar_init(&sm.scempty[i], kEpiWarps);
+    }
+    for (int i = 0; i < kAccPairs; ++i) {
+      mbar_init(&sm.acc_full[i], 1);
+      mbar_init(&sm.acc_empty[i], kEpiWarps);
+    }
+    mbar_init(&sm.mma_done, 1);
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&sm.tmem_base)),
+                 "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      pdl_wait();  // activations come from the upstream quantize kernel
+      int issued = 0, sc_issued = 0;
+      for (int s = 0; s < nstages; ++s) {
+        const int st = s % kStages, sc = s % kScSlots;
+        if (s >= kStages && !mbar_wait(&sm.empty[st], ((s / kStages) - 1) & 1, abort)) break;
+        if (s >= kScSlots && !mbar_wait(&sm.scempty[sc], ((s / kScSlots) - 1) & 1, abort)) break;
+        mbar_expect_tx(&sm.full[st], kAStageBytes + kB8StageBytes);
+        tma_load_2d(sm.a[st], &map_a, s * kBK, m0, &sm.full[st]);
+        tma_load_2d(sm.b8[st], &map_b, s * kBK, n0, &sm.full[st]);
+        issued = s + 1;
+        mbar_expect_tx(&sm.dxfull[sc], kDxStageBytes);
+        tma_load_2d(sm.dx[sc], &map_dx, m0, 2 * s, &sm.dxfull[sc]);
+        sc_issued = s + 1;
+      }
+      // Every copy this CTA issued must land before it can exit (on the normal path
+      // these waits return at once; after an abort they drain the copies).
+      volatile int no_abort = 0;
+      for (int s = (issued > kStages ? issued - kStages : 0); s < issued; ++s)
+        mbar_wait(&sm.full[s % kStages], (s / kStages) & 1, &no_abort);
+      for (int s = (sc_issued > kScSlots ? sc_issued - kScSlots : 0); s < sc_issued; ++s)
+        mbar_wait(&sm.dxfull[s % kScSlots], (s / kScSlots) & 1, &no_abort);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issue ----------------
+    if (lane == 0) {
+      for (int s = 0; s < nstages && !*abort; ++s) {
+        const int st = s % kStages, bs = s % kBSlots;
+        if (!mbar_wait(&sm.full[st], (s / kStages) & 1, abort)) break;
+        if (!mbar_wait(&sm.bfull[bs], (s / kBSlots) & 1, abort)) break;
+        tc_fence_after();
+        const uint64_t adesc = umma_desc_sw128(sm.a[st]);
+        const uint64_t bdesc = umma_desc_sw128(sm.b[bs]);
+        const int pr = s % kAccPairs;
+        if (s >= kAccPairs && !mbar_wait(&sm.acc_empty[pr], ((s / kAccPairs) - 1) & 1, abort)) break;
+        tc_fence_after();
+        for (int sub = 0; sub < 2; ++sub) {
+          if (2 * s + sub >= nb) break;
+          const uint32_t dcol = (uint32_t)(pr * 2 + sub) * kBN;
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) {
+            const uint64_t off = (uint64_t)((sub * 64 + kk * 32) >> 4);  // bytes along K within the 128 B row
+            umma_f16(tmem + dcol, adesc + off, bdesc + off, kk);
+          }
+        }
+        umma_commit(&sm.acc_full[pr]);
+        umma_commit(&sm.empty[st]);
+        umma_commit(&sm.bempty[bs]);
+      }
+      // all MMAs issued by this thread have completed before TMEM is released
+      umma_commit(&sm.mma_done);
+      volatile int no_abort = 0;
+      mbar_wait(&sm.mma_done, 0, &no_abort);
+    }
+    __syncwarp();
+  } else if (warp < 2 + kConvWarps) {
+    // ---------------- int8 -> f16 conversion, weight scales ----------------
+    const int ct = threadIdx.x - 64;  // 0..191
+    // Thread ct < kBN also owns the scales of weight row n0 + ct: it reads them 8 blocks
+    // (16 bytes) at a time, two groups ahead of the stage being converted, so no global
+    // load latency sits on the per-stage path.  A group index below ceil(nb/8) stays
+    // inside the row (its scale area is padded to 16 bytes).
+    const bool sload = ct < kBN && n0 + ct < N;
+    const int ngroups = (nb + 7) / 8;
+    const uint8_t* sbase = W + (size_t)(sload ? n0 + ct : 0) * S + K;
+    const int4 z4 = make_int4(0, 0, 0, 0);
+    int4 g0 = (sload && 0 < ngroups) ? ld_stream_v4(sbase) : z4;
+    int4 g1 = (sload && 1 < ngroups) ? ld_stream_v4(sbase + 16) : z4;
+    int4 g2 = (sload && 2 < ngroups) ? ld_stream_v4(sbase + 32) : z4;
+    for (int s = 0; s < nstages && !*abort; ++s) {
+      const int st = s % kStages, bs = s % kBSlots, sc = s % kScSlots;
+      if ((s & 3) == 0 && s > 0) {
+        const int g = s >> 2;
+        g0 = g1;
+        g1 = g2;
+        g2 = (sload && g + 2 < ngroups) ? ld_stream_v4(sbase + 16 * (g + 2)) : z4;
+      }
+      // weight scales -> scale ring (generic stores, read by the epilogue)
+      if (s >= kScSlots && !mbar_wait(&sm.scempty[sc], ((s / kScSlots) - 1) & 1, abort)) break;
+      if (ct < kBN) {
+        // scales of blocks 2s and 2s + 1: halves 2(s%4) and 2(s%4)+1 of group s/4
+        const int q = s & 3;
+        const uint32_t two = (uint32_t)(q == 0 ? g0.x : q == 1 ? g0.y : q == 2 ? g0.z : g0.w);
+        sm.dw[sc][0][ct] = __half2float(__ushort_as_half((unsigned short)(two & 0xffff)));
+        sm.dw[sc][1][ct] = (2 * s + 1 < nb) ? __half2float(__ushort_as_half((unsigned short)(two >> 16))) : 0.0f;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.dwfull[sc]);
+      // int8 -> f16 of the weight tile (16-byte output chunk of 8 values per item)
+      if (!mbar_wait(&sm.full[st], (s / kStages) & 1, abort)) break;
+      if (s >= kBSlots && !mbar_wait(&sm.bempty[bs], ((s / kBSlots) - 1) & 1, abort)) break;
+      for (int it = ct; it < kBN * 8; it += kConvThreads) {
+        const int r = it >> 3, c = it & 7;
+        const uint2 src = *reinterpret_cast<const uint2*>(sm.b8[st] + r * kBK + c * 8);
+        const uint2 lo = i8x4_to_f16x4(src.x);
+        const uint2 hi = i8x4_to_f16x4(src.y);
+        uint8_t* dst = sm.b[bs] + r * 128 + ((c ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.bfull[bs]);
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int ew = warp - (2 + kConvWarps);
+    const int quad = warp & 3;
+    const int half = ew >> 2;
+    const int m = m0 + quad * 32 + lane;
+    const bool mvalid = m < M;
+    pdl_wait();  // y may still be read by the upstream kernel; write it only after the wait
+    float2 acc[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.f, 0.f);
+    for (int s = 0; s < nstages && !*abort; ++s) {
+      const int sc = s % kScSlots;
+      if (!mbar_wait(&sm.dxfull[sc], (s / kScSlots) & 1, abort)) break;
+      if (!mbar_wait(&sm.dwfull[sc], (s / kScSlots) & 1, abort)) break;
+      const int pr = s % kAccPairs;
+      if (!mbar_wait(&sm.acc_full[pr], (s / kAccPairs) & 1, abort)) break;
+      tc_fence_after();
+      const int nsub = (2 * s + 1 < nb) ? 2 : 1;
+      for (int sub = 0; sub < nsub; ++sub) {
+        const float dxm = sm.dx[sc][sub][quad * 32 + lane];
+        const float2 dxx = make_float2(dxm, dxm);
+        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(pr * 2 + sub) * kBN + half * 64;
+        const float4* dwp = reinterpret_cast<const float4*>(&sm.dw[sc][sub][half * 64]);
+        // two groups of 32 columns: two x16 loads in flight per wait
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          float iv[32];
+          tmem_ld16_issue(taddr + h2 * 32, iv);
+          tmem_ld16_issue(taddr + h2 * 32 + 16, iv + 16);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if (h2 == 1 && sub == nsub - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.acc_empty[pr]);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 w4 = dwp[h2 * 8 + j];  // broadcast: every lane reads the same 16 bytes
+            const float2 s0 = f2_mul(make_float2(w4.x, w4.y), dxx);
+            const float2 s1 = f2_mul(make_float2(w4.z, w4.w), dxx);
+            acc[h2 * 16 + 2 * j] = f2_fma(make_float2(iv[4 * j], iv[4 * j + 1]), s0, acc[h2 * 16 + 2 * j]);
+            acc[h2 * 16 + 2 * j + 1] =
+                f2_fma(make_float2(iv[4 * j + 2], iv[4 * j + 3]), s1, acc[h2 * 16 + 2 * j + 1]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.scempty[sc]);
+    }
+    if (mvalid && !*abort) {
+      const int nbase = n0 + half * 64;
+      float* yr = y + (size_t)m * N + nbase;
+      if ((N & 3) == 0 && nbase + 64 <= N) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          reinterpret_cast<float4*>(yr)[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (nbase + 2 * j < N) yr[2 * j] = acc[j].x;
+          if (nbase + 2 * j + 1 < N) yr[2 * j + 1] = acc[j].y;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// Quantize x rows for the tensor-core path: f16 integers [M][K] and transposed f32
+// scales dxT[K/32][Mp] (rows padded to Mp = round_up(M, 4) so every row of the scale
+// tensor starts on 16 bytes, as TMA requires).  Thread i handles block b = i / M of
+// row m = i % M, so consecutive threads write consecutive scales.
+__global__ void quantize_rows_f16t_kernel(const float* __restrict__ x, int M, int Mp, int K,
+                                          __half* __restrict__ qh, float* __restrict__ dxT) {
+  const int nb = K >> 5;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  if (i < (int64_t)M * nb) {
+    const int b = (int)(i / M), m = (int)(i % M);
+    const float4* src = reinterpret_cast<const float4*>(x + (size_t)m * K + (size_t)b * kQK);
+    float4 v[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) v[t] = __ldg(src + t);
+    int q[8];
+    __half dh;
+    quantize_block_regs(v, q, dh);
+    uint4* dst = reinterpret_cast<uint4*>(qh + (size_t)m * K + (size_t)b * kQK);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const uint2 a = i8x4_to_f16x4((uint32_t)q[2 * t]);
+      const uint2 c = i8x4_to_f16x4((uint32_t)q[2 * t + 1]);
+      dst[t] = make_uint4(a.x, a.y, c.x, c.y);
+    }
+    dxT[(size_t)b * Mp + m] = __half2float(dh);
+  }
+  pdl_launch_dependents();
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (EncodeTiledFn) nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, void* base, uint64_t d0, uint64_t d1,
+               uint64_t stride1_bytes, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {d0, d1};
+  const cuuint64_t strides[1] = {stride1_bytes};
+  const cuuint32_t box[2] = {b0, b1};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, type, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline int64_t padded_rows(int64_t m) { return (m + 3) / 4 * 4; }
+
+}  // namespace
+
+size_t gemm_tc_smem_bytes() { return sizeof(Smem) + 1024; }
+
+size_t gemm_tc_workspace_bytes(int64_t m, int64_t k) {
+  const size_t qh = ((size_t)(m * k) * 2 + 255) / 256 * 256;
+  const size_t dx = ((size_t)(padded_rows(m) * (k / kQK)) * 4 + 255) / 256 * 256;
+  return qh + dx;
+}
+
+cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
+                           cudaStream_t s) {
+  const int M = (int)m, K = (int)w.k, N = (int)w.n;
+  const int Mp = (int)padded_rows(m);
+  const int nb = K / kQK;
+  __half* qh = static_cast<__half*>(workspace);
+  float* dxT = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((size_t)M * K * 2 + 255) / 256 * 256);
+
+  CUtensorMap map_a, map_b, map_dx;
+  if (!encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, qh, K, M, (uint64_t)K * 2, kBK, kBM,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, K, N, (uint64_t)w.row_stride, kBK, kBN,
+                 CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_2d(&map_dx, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dxT, M, nb, (uint64_t)Mp * 4, kBM, 2,
+                 CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+
+  // 1. quantize
+  {
+    const int64_t work = (int64_t)M * nb;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((work + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, quantize_rows_f16t_kernel, x, M, Mp, K, qh, dxT);
+    if (e != cudaSuccess) return e;
+  }
+  // 2. tensor-core matmul
+  const size_t smem = gemm_tc_smem_bytes();
+  static int configured[128] = {0};
+  const int dev = (w.device >= 0 && w.device < 128) ? w.device : 0;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_q8_0_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured[dev] = 1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemm_q8_0_tc_kernel, map_a, map_b, map_dx, (const uint8_t*)w.packed, w.row_stride,
+                            N, K, y, M);
+}
+
+cudaError_t read_tc_fault(unsigned int* flags, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(flags, g_tc_fault, sizeof(unsigned int));
+  if (e == cudaSuccess && clear) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_tc_fault, &z, sizeof(z));
+  }
+  return e;
+}
+
+}  // namespace q8lin

@@ -42,6 +42,13 @@ cudaError_t launch_gemv(const q8lin_weight& w, const float* x, float* y, int m,
 cudaError_t launch_gemm(const q8lin_weight& w, const int8_t* qx, const float* dx, float* y,
                         int64_t m, cudaStream_t s);
 
+// Tensor-core batched path (gemm_tc.cu): quantize x to f16 integers + transposed
+// scales in `workspace`, then the tcgen05 matmul.
+size_t gemm_tc_workspace_bytes(int64_t m, int64_t k);
+cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
+                           cudaStream_t s);
+cudaError_t read_tc_fault(unsigned int* flags, bool clear);
+
 int sm_count(int device);
 
 // Programmatic dependent launch on/off (env Q8LIN_PDL=0 turns it off; read once).

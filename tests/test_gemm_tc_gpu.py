@@ -1,0 +1,62 @@
+"""The tensor-core batched path (M > 16) against the oracle, plus an exact-integer check."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from talechime_b200 import QMatMul, _lib, synth
+from tests.conftest import assert_close_to_oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(oracle_lib, dev, seed, m, k, n):
+    x, w = synth.case(seed, m, k, n)
+    y_ref = oracle_lib.matmul(x, w, n, threads=16)
+    q = QMatMul.from_gguf_blocks(w, n, k, device=dev)
+    y = q.forward(torch.from_numpy(x).to(dev))
+    torch.cuda.synchronize()
+    return assert_close_to_oracle(y.cpu().numpy(), y_ref)
+
+
+@pytest.mark.parametrize("m,k,n", [
+    (17, 64, 128),      # one stage, partial M tile
+    (33, 96, 130),      # odd block count (pad block), partial N tile
+    (128, 2048, 256),   # exact tiles
+    (200, 544, 300),    # 17 blocks, ragged everything
+    (64, 6144, 256),    # long K (down projection)
+])
+def test_tc_matches_oracle(oracle_lib, cuda_device, m, k, n):
+    _run(oracle_lib, cuda_device, 300 + m + k + n, m, k, n)
+
+
+def test_tc_sweep_shape_m256(oracle_lib, cuda_device):
+    _run(oracle_lib, cuda_device, 401, 256, 2048, 2048)
+
+
+def test_tc_integer_products_are_exact(cuda_device):
+    """Unit scales: x holds integers with |x| <= 127 and amax 127 in every block, so the
+    activation scale is exactly 1 and y is an exact integer dot product."""
+    rng = np.random.default_rng(77)
+    m, k, n = 130, 256, 136
+    x = rng.integers(-126, 127, size=(m, k)).astype(np.float32)
+    x.reshape(m, k // 32, 32)[:, :, 0] = 127.0  # every block has amax 127 -> d = 1
+    qs = rng.integers(-127, 128, size=(n, k // 32, 32), dtype=np.int8)
+    blocks = np.empty((n, k // 32, 34), dtype=np.uint8)
+    blocks[:, :, 0:2] = np.full((n, k // 32), 1.0, dtype=np.float16).view(np.uint8).reshape(n, k // 32, 2)
+    blocks[:, :, 2:] = qs.view(np.uint8)
+    q = QMatMul.from_gguf_blocks(blocks, n, k, device=cuda_device)
+    y = q.forward(torch.from_numpy(x).to(cuda_device)).cpu().numpy()
+    ref = x.astype(np.int64) @ qs.reshape(n, k).astype(np.int64).T
+    assert np.array_equal(y.astype(np.int64), ref)
+    assert np.abs(ref).max() < 2 ** 24  # so the f32 result is exact
+
+
+def test_tc_fault_word_clear(cuda_device):
+    _, w = synth.case(402, 1, 128, 64)
+    q = QMatMul.from_gguf_blocks(w, 64, 128, device=cuda_device)
+    q.forward(torch.randn((40, 128), device=cuda_device))
+    flags = ctypes.c_uint32(123)
+    _lib.check(_lib.lib().q8lin_fault_status(0, ctypes.byref(flags), 1))
+    assert flags.value == 0
