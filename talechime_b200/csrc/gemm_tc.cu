@@ -1,33 +1,35 @@
 // Batched Q8_0 matmul on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
-// y[m][n] = sum_b dw[n][b] * dx[m][b] * I[m][n][b],  I = exact int dot of one 32-value
+// y[m][n] = sum_b dx[m][b] * dw[n][b] * I[m][n][b],  I = exact int dot of one 32-value
 // block.  The per-block scales forbid accumulating across blocks inside the MMA, so
-// every 32-value block gets its own tensor-core product and the rescale happens in
+// every 32-value block gets its own tensor-core products and the rescale happens in
 // registers:
 //   * A = activations (MMA M = 128 rows of x), f16 holding the exact Q8_0 integers
 //     (written by quantize_rows_f16t), 128B-swizzled tiles loaded by TMA;
 //   * B = weights (MMA N = 128 rows of W), int8 tiles loaded by TMA from the packed
 //     plane and widened to f16 integers in shared memory by converter warps (same
 //     swizzled K-major layout);
-//   * per block: two tcgen05.mma kind::f16 (K = 16 each) into a fresh TMEM buffer
-//     (f32; products of |q| <= 127 and their 32-term sums are exact integers);
-//   * epilogue warps read the block's 128x128 result with tcgen05.ld and accumulate
-//     acc += I * (dw * dx) in f32 registers (packed f32x2 math); TMEM holds two
-//     stages' worth of block results (4 x 128 columns), handed over a stage at a time,
-//     so the MMAs of stage s+1 run while stage s is rescaled.
-// One CTA owns a 128 (m) x 128 (n) output tile over the whole K.
+//   * per block: two tcgen05.mma kind::f16 (K = 16 each) give I in a TMEM buffer (f32;
+//     products of |q| <= 127 and their 32-term sums are exact integers), and a third
+//     MMA gives the scale product P[m][n] = dx[m] * dw[n] next to it: its operands are
+//     K = 16 tiles whose only non-zero column holds the f16 scales, so P is the outer
+//     product, exact in f32 (11-bit x 11-bit significands);
+//   * epilogue warps read I and P with tcgen05.ld and accumulate acc += I * P with
+//     packed f32x2 FMAs: no shared-memory traffic and no broadcast of scales per
+//     column, which is what bounds a register-side rescale.
+// TMEM holds two blocks (2 x (I + P) = 512 columns), so the MMAs of block b + 1 run
+// while block b is rescaled.  One CTA owns a 128 (m) x 128 (n) output tile over all K.
 //
-// Three rings keep the loads far ahead of the math (a stage = 64 K values = 2 blocks):
-//   operand ring (kStages): A f16 tile + B int8 tile, freed by the MMA commit;
-//   f16 weight ring (2 slots): converted B, freed by the MMA commit;
-//   scale ring (kScSlots): activation scales (TMA) + weight scales (converters),
-//     freed by the epilogue.
+// Rings (a stage = 64 K values = 2 blocks):
+//   operand ring (kStages): A f16 tile + B int8 tile + activation scales;
+//   converted ring (2 slots): f16 weight tile + the two blocks' scale operands;
+//   one MMA commit per stage (consumed[s % kStages]) frees both slots of stage s.
 //
-// Warp roles (512 threads):
+// Warp roles (448 threads):
 //   warp 0      TMA producer (waits on the upstream kernel before loading activations)
 //   warp 1      TMEM allocation and MMA issue (one elected lane)
-//   warps 2-7   int8 -> f16 conversion of the weight tile, weight scales -> smem
-//   warps 8-15  epilogue: TMEM lane quadrant (warp % 4) x column half ((warp - 8) / 4)
+//   warps 2-5   int8 -> f16 conversion of the weight tile; scale operands
+//   warps 6-13  epilogue: TMEM lane quadrant (warp % 4) x 64-column half ((warp - 6) / 4)
 //
 // Every mbarrier wait is bounded; a wait that runs out sets a fault word that the host
 // reads with q8lin_fault_status and makes the CTA drain and return.
@@ -46,37 +48,37 @@ constexpr int kBM = 128;          // activation rows per tile (MMA M)
 constexpr int kBN = 128;          // weight rows per tile (MMA N)
 constexpr int kBK = 64;           // K values per stage (two Q8_0 blocks)
 constexpr int kStages = 6;        // operand ring
-constexpr int kBSlots = 2;        // converted-weight ring
-constexpr int kScSlots = 8;       // scale ring
-constexpr int kThreads = 512;
-constexpr int kConvWarps = 6;     // warps 2..7
+constexpr int kBSlots = 2;        // converted ring
+constexpr int kConvWarps = 4;     // warps 2..5
 constexpr int kConvThreads = kConvWarps * 32;
-constexpr int kEpiWarps = 8;
-constexpr int kAccBufs = 4;       // TMEM block buffers (4 x 128 columns = all of TMEM), used in pairs
-constexpr int kAccPairs = kAccBufs / 2;
-constexpr uint32_t kTmemCols = kAccBufs * kBN;
+constexpr int kEpiWarps = 8;      // warps 6..13
+constexpr int kEpiCols = kBN / (kEpiWarps / 4);  // TMEM columns per epilogue warp
+constexpr int kEpiWarp0 = 2 + kConvWarps;
+constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
+constexpr uint32_t kTmemCols = 512;  // two blocks x (I: kBN columns + P: kBN columns)
 constexpr uint32_t kSpinLimit = 1u << 24;
 
 constexpr int kAStageBytes = kBM * kBK * 2;   // 16 KB f16
 constexpr int kBStageBytes = kBN * kBK * 2;   // 16 KB f16
 constexpr int kB8StageBytes = kBN * kBK;      //  8 KB int8
 constexpr int kDxStageBytes = 2 * kBM * 4;    //  1 KB f32
+constexpr int kScaleTileBytes = 128 * 16 * 2; //  4 KB: 128 rows x K = 16 f16, no swizzle
+
+static_assert(kConvThreads == kBN && kConvThreads == kBM, "one converter thread per tile row");
 
 struct Smem {
   alignas(1024) uint8_t a[kStages][kAStageBytes];
   alignas(1024) uint8_t b[kBSlots][kBStageBytes];
+  alignas(1024) uint8_t sx[kBSlots][2][kScaleTileBytes];  // activation-scale operand of each block
+  alignas(1024) uint8_t sw[kBSlots][2][kScaleTileBytes];  // weight-scale operand of each block
   alignas(128) uint8_t b8[kStages][kB8StageBytes];
-  alignas(128) float dx[kScSlots][2][kBM];  // activation scales of a stage's two blocks (TMA)
-  alignas(16) float dw[kScSlots][2][kBN];   // weight scales of a stage's two blocks
-  alignas(8) uint64_t full[kStages];        // A + B int8 landed
-  alignas(8) uint64_t empty[kStages];       // MMAs of the stage done (operands free)
-  alignas(8) uint64_t bfull[kBSlots];       // converted B written
-  alignas(8) uint64_t bempty[kBSlots];      // MMAs reading the converted B done
-  alignas(8) uint64_t dxfull[kScSlots];     // activation scales landed (TMA)
-  alignas(8) uint64_t dwfull[kScSlots];     // weight scales written (converter warps)
-  alignas(8) uint64_t scempty[kScSlots];    // epilogue done with the scales
-  alignas(8) uint64_t acc_full[kAccPairs];  // a stage's block results ready in a TMEM buffer pair
-  alignas(8) uint64_t acc_empty[kAccPairs]; // epilogue done reading the pair
+  alignas(128) float dx[kStages][2][kBM];   // activation scales of a stage's two blocks (TMA)
+  alignas(8) uint64_t full[kStages];        // A + B int8 + activation scales landed
+  alignas(8) uint64_t consumed[kStages];    // MMAs of stage s done: its operand slot and its
+                                            // converted slot are free (one commit serves both)
+  alignas(8) uint64_t bfull[kBSlots];       // converted B and scale operands written
+  alignas(8) uint64_t acc_full[2];          // a block's I and P ready in TMEM buffer j
+  alignas(8) uint64_t acc_empty[2];         // epilogue done reading buffer j
   alignas(8) uint64_t mma_done;             // every MMA this CTA issued has completed
   uint32_t tmem_base;
   int abort;
@@ -107,6 +109,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
   atomicOr(&g_tc_fault, 1u);
   return false;
 }
+// Every lane waits (and so acquires); the verdict is made warp-uniform.
+__device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
+  return __all_sync(0xffffffffu, mbar_wait(b, parity, abort));
+}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
   asm volatile(
@@ -127,22 +133,40 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(const void* base) {
   return d;
 }
 
+// K-major, unswizzled descriptor of a scale tile: core matrices of 8 rows x 16 B stored
+// as 128 contiguous bytes; the two core matrices along K are 128 B apart (leading byte
+// offset) and consecutive 8-row groups 256 B apart (stride byte offset).
+__device__ __forceinline__ uint64_t umma_desc_plain(const void* base) {
+  const uint64_t addr = su32(base);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;
+  d |= (uint64_t)(128 >> 4) << 16;
+  d |= (uint64_t)(256 >> 4) << 32;
+  d |= (uint64_t)1 << 46;                 // layout field 0: no swizzle
+  return d;
+}
+// Byte offset of element (row r, k = 0) in a scale tile.
+__device__ __forceinline__ uint32_t scale_tile_offset(int r) { return (uint32_t)((r >> 3) * 256 + (r & 7) * 16); }
+
 // Instruction descriptor: kind::f16, A/B f16, D f32, both K-major, M = 128, N = kBN.
 constexpr uint32_t kIdesc = (1u << 4)                    // D format f32
                           | (0u << 7) | (0u << 10)       // A, B f16
                           | ((uint32_t)(kBN >> 3) << 17)  // N >> 3
                           | ((uint32_t)(kBM >> 4) << 24); // M >> 4
 
+// MMA and commit are called by a converged warp; one elected lane issues them.
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
   asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+      "{\n .reg .pred p, e;\n elect.sync _|e, 0xffffffff;\n setp.ne.b32 p, %4, 0;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
       ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
-               : "memory");
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}" ::"r"(su32(bar))
+      : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -159,12 +183,6 @@ __device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, float* v) {
       : "memory");
 }
 
-__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
-  float2 d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(reinterpret_cast<uint64_t&>(d))
-      : "l"(reinterpret_cast<const uint64_t&>(a)), "l"(reinterpret_cast<const uint64_t&>(b)));
-  return d;
-}
 __device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
   float2 d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(reinterpret_cast<uint64_t&>(d))
@@ -205,24 +223,27 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1);
+      mbar_init(&sm.consumed[i], 1);
     }
-    for (int i = 0; i < kBSlots; ++i) {
-      mbar_init(&sm.bfull[i], kConvWarps);
-      mbar_init(&sm.bempty[i], 1);
-    }
-    for (int i = 0; i < kScSlots; ++i) {
-      mbar_init(&sm.dxfull[i], 1);
-      mbar_init(&sm.dwfull[i], kConvWarps);
-      mbar_init(&sm.scempty[i], kEpiWarps);
-    }
-    for (int i = 0; i < kAccPairs; ++i) {
+    for (int i = 0; i < kBSlots; ++i) mbar_init(&sm.bfull[i], kConvWarps);
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.acc_full[i], 1);
       mbar_init(&sm.acc_empty[i], kEpiWarps);
     }
     mbar_init(&sm.mma_done, 1);
     sm.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // The scale tiles are zero except column 0, which the converters rewrite per block.
+  {
+    uint4* zx = reinterpret_cast<uint4*>(&sm.sx[0][0][0]);
+    uint4* zw = reinterpret_cast<uint4*>(&sm.sw[0][0][0]);
+    constexpr int kN16 = (int)(sizeof(Smem::sx) / 16);
+    for (int i = threadIdx.x; i < kN16; i += kThreads) {
+      zx[i] = make_uint4(0, 0, 0, 0);
+      zw[i] = make_uint4(0, 0, 0, 0);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&sm.tmem_base)),
@@ -238,167 +259,164 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       pdl_wait();  // activations come from the upstream quantize kernel
-      int issued = 0, sc_issued = 0;
+      int issued = 0;
       for (int s = 0; s < nstages; ++s) {
-        const int st = s % kStages, sc = s % kScSlots;
-        if (s >= kStages && !mbar_wait(&sm.empty[st], ((s / kStages) - 1) & 1, abort)) break;
-        if (s >= kScSlots && !mbar_wait(&sm.scempty[sc], ((s / kScSlots) - 1) & 1, abort)) break;
-        mbar_expect_tx(&sm.full[st], kAStageBytes + kB8StageBytes);
+        const int st = s % kStages;
+        if (s >= kStages && !mbar_wait(&sm.consumed[st], ((s / kStages) - 1) & 1, abort)) break;
+        mbar_expect_tx(&sm.full[st], kAStageBytes + kB8StageBytes + kDxStageBytes);
         tma_load_2d(sm.a[st], &map_a, s * kBK, m0, &sm.full[st]);
         tma_load_2d(sm.b8[st], &map_b, s * kBK, n0, &sm.full[st]);
+        tma_load_2d(sm.dx[st], &map_dx, m0, 2 * s, &sm.full[st]);
         issued = s + 1;
-        mbar_expect_tx(&sm.dxfull[sc], kDxStageBytes);
-        tma_load_2d(sm.dx[sc], &map_dx, m0, 2 * s, &sm.dxfull[sc]);
-        sc_issued = s + 1;
       }
       // Every copy this CTA issued must land before it can exit (on the normal path
       // these waits return at once; after an abort they drain the copies).
       volatile int no_abort = 0;
       for (int s = (issued > kStages ? issued - kStages : 0); s < issued; ++s)
         mbar_wait(&sm.full[s % kStages], (s / kStages) & 1, &no_abort);
-      for (int s = (sc_issued > kScSlots ? sc_issued - kScSlots : 0); s < sc_issued; ++s)
-        mbar_wait(&sm.dxfull[s % kScSlots], (s / kScSlots) & 1, &no_abort);
     }
   } else if (warp == 1) {
     // ---------------- MMA issue ----------------
-    if (lane == 0) {
-      for (int s = 0; s < nstages && !*abort; ++s) {
-        const int st = s % kStages, bs = s % kBSlots;
-        if (!mbar_wait(&sm.full[st], (s / kStages) & 1, abort)) break;
-        if (!mbar_wait(&sm.bfull[bs], (s / kBSlots) & 1, abort)) break;
-        tc_fence_after();
-        const uint64_t adesc = umma_desc_sw128(sm.a[st]);
-        const uint64_t bdesc = umma_desc_sw128(sm.b[bs]);
-        const int pr = s % kAccPairs;
-        if (s >= kAccPairs && !mbar_wait(&sm.acc_empty[pr], ((s / kAccPairs) - 1) & 1, abort)) break;
-        tc_fence_after();
-        for (int sub = 0; sub < 2; ++sub) {
-          if (2 * s + sub >= nb) break;
-          const uint32_t dcol = (uint32_t)(pr * 2 + sub) * kBN;
-#pragma unroll
-          for (int kk = 0; kk < 2; ++kk) {
-            const uint64_t off = (uint64_t)((sub * 64 + kk * 32) >> 4);  // bytes along K within the 128 B row
-            umma_f16(tmem + dcol, adesc + off, bdesc + off, kk);
-          }
+    // The whole warp runs the loop and waits; one elected lane issues each MMA and
+    // commit.  Issuing from a converged warp with straight-line descriptor arithmetic
+    // keeps the issue cost of one 128x128x16 MMA near its 64-cycle execution time.
+    for (int s = 0; s < nstages; ++s) {
+      const int st = s % kStages, bs = s % kBSlots;
+      if (!warp_wait(&sm.full[st], (s / kStages) & 1, abort)) break;
+      if (!warp_wait(&sm.bfull[bs], (s / kBSlots) & 1, abort)) break;
+      tc_fence_after();
+      const uint64_t adesc = umma_desc_sw128(sm.a[st]);
+      const uint64_t bdesc = umma_desc_sw128(sm.b[bs]);
+      bool stop = false;
+      // block 2s + sub goes to TMEM buffer sub: I in columns [256 sub, 256 sub + 128),
+      // P in the next 128.  K offsets within the 128 B swizzled row: 64 B per block,
+      // 32 B per MMA.
+      for (int sub = 0; sub < 2; ++sub) {
+        if (2 * s + sub >= nb) break;
+        if (s >= 1 && !warp_wait(&sm.acc_empty[sub], (s - 1) & 1, abort)) {
+          stop = true;
+          break;
         }
-        umma_commit(&sm.acc_full[pr]);
-        umma_commit(&sm.empty[st]);
-        umma_commit(&sm.bempty[bs]);
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)sub * 2 * kBN;
+        const uint64_t off = (uint64_t)(sub * 4);
+        umma_f16(d, adesc + off, bdesc + off, 0);
+        umma_f16(d, adesc + off + 2, bdesc + off + 2, 1);
+        umma_f16(d + kBN, umma_desc_plain(sm.sx[bs][sub]), umma_desc_plain(sm.sw[bs][sub]), 0);
+        umma_commit(&sm.acc_full[sub]);
       }
-      // all MMAs issued by this thread have completed before TMEM is released
-      umma_commit(&sm.mma_done);
-      volatile int no_abort = 0;
-      mbar_wait(&sm.mma_done, 0, &no_abort);
+      umma_commit(&sm.consumed[st]);
+      if (stop) break;
     }
-    __syncwarp();
-  } else if (warp < 2 + kConvWarps) {
-    // ---------------- int8 -> f16 conversion, weight scales ----------------
-    const int ct = threadIdx.x - 64;  // 0..191
-    // Thread ct < kBN also owns the scales of weight row n0 + ct: it reads them 8 blocks
-    // (16 bytes) at a time, two groups ahead of the stage being converted, so no global
-    // load latency sits on the per-stage path.  A group index below ceil(nb/8) stays
-    // inside the row (its scale area is padded to 16 bytes).
-    const bool sload = ct < kBN && n0 + ct < N;
+    // all MMAs this warp issued have completed before TMEM is released
+    umma_commit(&sm.mma_done);
+    volatile int no_abort = 0;
+    warp_wait(&sm.mma_done, 0, &no_abort);
+  } else if (warp < kEpiWarp0) {
+    // ---------------- int8 -> f16 conversion, scale operands ----------------
+    const int ct = threadIdx.x - 64;  // 0..127: also the weight row n0 + ct and activation row m0 + ct
+    // Thread ct reads the scales of weight row n0 + ct 8 blocks (16 bytes) at a time, two
+    // groups ahead of the stage being converted, so no global load latency sits on the
+    // per-stage path.  A group index below ceil(nb/8) stays inside the row (its scale
+    // area is padded to 16 bytes).
+    const bool sload = n0 + ct < N;
     const int ngroups = (nb + 7) / 8;
     const uint8_t* sbase = W + (size_t)(sload ? n0 + ct : 0) * S + K;
     const int4 z4 = make_int4(0, 0, 0, 0);
     int4 g0 = (sload && 0 < ngroups) ? ld_stream_v4(sbase) : z4;
     int4 g1 = (sload && 1 < ngroups) ? ld_stream_v4(sbase + 16) : z4;
     int4 g2 = (sload && 2 < ngroups) ? ld_stream_v4(sbase + 32) : z4;
+    const uint32_t soff = scale_tile_offset(ct);
     for (int s = 0; s < nstages && !*abort; ++s) {
-      const int st = s % kStages, bs = s % kBSlots, sc = s % kScSlots;
+      const int st = s % kStages, bs = s % kBSlots;
       if ((s & 3) == 0 && s > 0) {
         const int g = s >> 2;
         g0 = g1;
         g1 = g2;
         g2 = (sload && g + 2 < ngroups) ? ld_stream_v4(sbase + 16 * (g + 2)) : z4;
       }
-      // weight scales -> scale ring (generic stores, read by the epilogue)
-      if (s >= kScSlots && !mbar_wait(&sm.scempty[sc], ((s / kScSlots) - 1) & 1, abort)) break;
-      if (ct < kBN) {
-        // scales of blocks 2s and 2s + 1: halves 2(s%4) and 2(s%4)+1 of group s/4
-        const int q = s & 3;
-        const uint32_t two = (uint32_t)(q == 0 ? g0.x : q == 1 ? g0.y : q == 2 ? g0.z : g0.w);
-        sm.dw[sc][0][ct] = __half2float(__ushort_as_half((unsigned short)(two & 0xffff)));
-        sm.dw[sc][1][ct] = (2 * s + 1 < nb) ? __half2float(__ushort_as_half((unsigned short)(two >> 16))) : 0.0f;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.dwfull[sc]);
-      // int8 -> f16 of the weight tile (16-byte output chunk of 8 values per item)
       if (!mbar_wait(&sm.full[st], (s / kStages) & 1, abort)) break;
-      if (s >= kBSlots && !mbar_wait(&sm.bempty[bs], ((s / kBSlots) - 1) & 1, abort)) break;
-      for (int it = ct; it < kBN * 8; it += kConvThreads) {
-        const int r = it >> 3, c = it & 7;
-        const uint2 src = *reinterpret_cast<const uint2*>(sm.b8[st] + r * kBK + c * 8);
-        const uint2 lo = i8x4_to_f16x4(src.x);
-        const uint2 hi = i8x4_to_f16x4(src.y);
+      // converted slot bs is free once the MMAs of stage s - kBSlots are done
+      if (s >= kBSlots) {
+        const int sp = s - kBSlots;
+        if (!mbar_wait(&sm.consumed[sp % kStages], (sp / kStages) & 1, abort)) break;
+      }
+      // weight tile: 16-byte output chunk (8 values) per item, all loads first
+      constexpr int kItems = kBN * 8 / kConvThreads;
+      uint2 src[kItems];
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) {
+        const int it = ct + i * kConvThreads;
+        src[i] = *reinterpret_cast<const uint2*>(sm.b8[st] + (it >> 3) * kBK + (it & 7) * 8);
+      }
+#pragma unroll
+      for (int i = 0; i < kItems; ++i) {
+        const int it = ct + i * kConvThreads, r = it >> 3, c = it & 7;
+        const uint2 lo = i8x4_to_f16x4(src[i].x);
+        const uint2 hi = i8x4_to_f16x4(src[i].y);
         uint8_t* dst = sm.b[bs] + r * 128 + ((c ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = make_uint4(lo.x, lo.y, hi.x, hi.y);
       }
+      // scale operands of blocks 2s and 2s + 1: weight scales are halves 2(s%4) and
+      // 2(s%4)+1 of group s/4 (raw f16 bits); activation scales are f16 values held as f32
+      const int q = s & 3;
+      const uint32_t two = (uint32_t)(q == 0 ? g0.x : q == 1 ? g0.y : q == 2 ? g0.z : g0.w);
+      *reinterpret_cast<uint16_t*>(sm.sw[bs][0] + soff) = (uint16_t)(two & 0xffffu);
+      *reinterpret_cast<uint16_t*>(sm.sw[bs][1] + soff) = (2 * s + 1 < nb) ? (uint16_t)(two >> 16) : (uint16_t)0;
+      *reinterpret_cast<__half*>(sm.sx[bs][0] + soff) = __float2half_rn(sm.dx[st][0][ct]);
+      *reinterpret_cast<__half*>(sm.sx[bs][1] + soff) = __float2half_rn(sm.dx[st][1][ct]);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.bfull[bs]);
     }
   } else {
     // ---------------- epilogue ----------------
-    const int ew = warp - (2 + kConvWarps);
+    const int ew = warp - kEpiWarp0;
     const int quad = warp & 3;
-    const int half = ew >> 2;
+    const int cg = ew >> 2;  // column group: kEpiCols columns of the tile
     const int m = m0 + quad * 32 + lane;
     const bool mvalid = m < M;
     pdl_wait();  // y may still be read by the upstream kernel; write it only after the wait
-    float2 acc[32];
+    float2 acc[kEpiCols / 2];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.f, 0.f);
+    for (int j = 0; j < kEpiCols / 2; ++j) acc[j] = make_float2(0.f, 0.f);
     for (int s = 0; s < nstages && !*abort; ++s) {
-      const int sc = s % kScSlots;
-      if (!mbar_wait(&sm.dxfull[sc], (s / kScSlots) & 1, abort)) break;
-      if (!mbar_wait(&sm.dwfull[sc], (s / kScSlots) & 1, abort)) break;
-      const int pr = s % kAccPairs;
-      if (!mbar_wait(&sm.acc_full[pr], (s / kAccPairs) & 1, abort)) break;
-      tc_fence_after();
-      const int nsub = (2 * s + 1 < nb) ? 2 : 1;
-      for (int sub = 0; sub < nsub; ++sub) {
-        const float dxm = sm.dx[sc][sub][quad * 32 + lane];
-        const float2 dxx = make_float2(dxm, dxm);
-        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(pr * 2 + sub) * kBN + half * 64;
-        const float4* dwp = reinterpret_cast<const float4*>(&sm.dw[sc][sub][half * 64]);
-        // two groups of 32 columns: two x16 loads in flight per wait
+      for (int sub = 0; sub < 2; ++sub) {
+        if (2 * s + sub >= nb) break;
+        if (!mbar_wait(&sm.acc_full[sub], s & 1, abort)) break;
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)sub * 2 * kBN + cg * kEpiCols;
+        // 32 columns of I and of P per TMEM wait
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          float iv[32];
-          tmem_ld16_issue(taddr + h2 * 32, iv);
-          tmem_ld16_issue(taddr + h2 * 32 + 16, iv + 16);
+        for (int c = 0; c < kEpiCols; c += 32) {
+          float iv[32], pv[32];
+          tmem_ld16_issue(taddr + c, iv);
+          tmem_ld16_issue(taddr + c + 16, iv + 16);
+          tmem_ld16_issue(taddr + kBN + c, pv);
+          tmem_ld16_issue(taddr + kBN + c + 16, pv + 16);
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-          if (h2 == 1 && sub == nsub - 1) {
+          if (c + 32 == kEpiCols) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sm.acc_empty[pr]);
+            if (lane == 0) mbar_arrive(&sm.acc_empty[sub]);
           }
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 w4 = dwp[h2 * 8 + j];  // broadcast: every lane reads the same 16 bytes
-            const float2 s0 = f2_mul(make_float2(w4.x, w4.y), dxx);
-            const float2 s1 = f2_mul(make_float2(w4.z, w4.w), dxx);
-            acc[h2 * 16 + 2 * j] = f2_fma(make_float2(iv[4 * j], iv[4 * j + 1]), s0, acc[h2 * 16 + 2 * j]);
-            acc[h2 * 16 + 2 * j + 1] =
-                f2_fma(make_float2(iv[4 * j + 2], iv[4 * j + 3]), s1, acc[h2 * 16 + 2 * j + 1]);
-          }
+          for (int p = 0; p < 16; ++p)
+            acc[c / 2 + p] = f2_fma(make_float2(iv[2 * p], iv[2 * p + 1]), make_float2(pv[2 * p], pv[2 * p + 1]),
+                                    acc[c / 2 + p]);
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.scempty[sc]);
     }
     if (mvalid && !*abort) {
-      const int nbase = n0 + half * 64;
+      const int nbase = n0 + cg * kEpiCols;
       float* yr = y + (size_t)m * N + nbase;
-      if ((N & 3) == 0 && nbase + 64 <= N) {
+      if ((N & 3) == 0 && nbase + kEpiCols <= N) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
+        for (int j = 0; j < kEpiCols / 4; ++j)
           reinterpret_cast<float4*>(yr)[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < kEpiCols / 2; ++j) {
           if (nbase + 2 * j < N) yr[2 * j] = acc[j].x;
           if (nbase + 2 * j + 1 < N) yr[2 * j + 1] = acc[j].y;
         }
