@@ -120,7 +120,8 @@ int q8lin_forward_noalloc(const q8lin_weight* w, const float* x, float* y, int64
 
 /*
  * Device-side fault word of `device` (bit 0: a tensor-core kernel's bounded wait ran
- * out and the kernel returned early; its output is then invalid).  Reads it with a
+ * out, bit 1: the M = 1 streaming GEMV's bounded wait ran out; the kernel returned
+ * early and its output is invalid).  Reads it with a
  * device synchronisation; `clear` resets it.  No counterpart in the reference (candle's
  * kernels have no bounded waits); this is the library's failure-detection hook.
  */

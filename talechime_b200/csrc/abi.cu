@@ -338,10 +338,11 @@ int q8lin_fault_status(int device, uint32_t* flags, int clear) {
   int st = check_device(device);
   if (st != Q8LIN_OK) return st;
   DeviceGuard guard(device);
-  unsigned int f = 0;
+  unsigned int f = 0, g = 0;
   cudaError_t e = read_tc_fault(&f, clear != 0);
+  if (e == cudaSuccess) e = read_gemv_fault(&g, clear != 0);
   if (e != cudaSuccess) return cuda_fail(e, "read fault word");
-  *flags = f;
+  *flags = f | g;
   return Q8LIN_OK;
 }
 

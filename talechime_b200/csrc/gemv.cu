@@ -1,13 +1,17 @@
 // Decode GEMV for 1 <= M <= 16: y[M][N] = Q8_0(x)[M][K] . W^T.
 //
 // HBM-bound: every launch streams the whole repacked weight (N*K*34/32 bytes) once.
-// Geometry: two 512-thread CTAs per SM; CTA c owns the contiguous weight rows
-// [N*c/G, N*(c+1)/G), its warps take those rows round-robin, and the 32 lanes of a
-// warp stride a row in 16-byte chunks (chunk c = half of block c/2) with 128-bit
-// streaming loads, four chunks in flight per lane and the next batch issued before
-// the current one is reduced.
+// Two kernels:
+//   * M = 1 and K <= 8192: gemv_q8_0_stream_kernel (below), one CTA per SM with a
+//     shared-memory ring filled by bulk copies, sized so the next linear's CTA is
+//     co-resident and prefetches its weights while this one computes;
+//   * otherwise gemv_q8_0_kernel: two 512-thread CTAs per SM; CTA c owns the contiguous
+//     weight rows [N*c/G, N*(c+1)/G), its warps take those rows round-robin, and the 32
+//     lanes of a warp stride a row in 16-byte chunks (chunk c = half of block c/2) with
+//     128-bit streaming loads, four chunks in flight per lane and the next batch issued
+//     before the current one is reduced.
 //
-// Dependent-launch structure (the kernel is launched with programmatic stream
+// Dependent-launch structure of gemv_q8_0_kernel (launched with programmatic stream
 // serialization):
 //   1. prologue -- weights are constant, so before griddepcontrol.wait every warp
 //      issues its first weight batch into registers.  This overlaps the upstream
@@ -155,6 +159,254 @@ gemv_q8_0_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K,
   }
 }
 
+// ---------------------------------------------------------------------------------
+// M = 1 streaming GEMV with cross-launch weight prefetch.
+//
+// Geometry: one CTA per SM owning the contiguous rows [r0, r1): 16 consumer warps and
+// one producer warp, at most 56 registers per thread and ~100 KB of shared memory, so
+// two CTAs fit on an SM -- the CTA of the next linear in the stream is resident while
+// this one runs.  The CTA's rows are one contiguous byte range of the packed plane,
+// copied into a shared-memory ring of `rpc`-row chunks with 1-D bulk copies
+// (cp.async.bulk, no multicast).
+//
+// Order of events:
+//   1. launch_dependents at once: the next linear's CTAs may become resident and start
+//      their own copies while this one computes;
+//   2. producer warp: copies of the first `slots` chunks -- weights are constant, so
+//      they are issued before the dependency wait and overlap the previous linear --
+//      then one refill per chunk whose rows have all been reduced (empty barrier);
+//   3. consumer warps: griddepcontrol.wait, x quantized to Q8_0 in shared memory, then
+//      each warp keeps its 2048-value segment of x (four 16-byte units per lane) and
+//      the block scales in registers.  A row of K values is reduced by
+//      ceil(K / 2048) warps, one segment each, straight from the ring; with several
+//      segments the partial sums meet in shared memory and the last warp to arrive
+//      adds them in segment order.  No CTA-wide barrier per chunk.
+// Each block term is ((f32(isum) * dw) * dx) rounded per product as candle's scalar
+// vec_dot; sums across blocks are trees, so outputs agree within f32 summation
+// tolerance.  Every wait is bounded: on timeout bit 1 of the fault word is set and the
+// waiting warp stops; the producer waits (bounded) for its last copies before it exits.
+constexpr int kConsumerWarps = 16;
+constexpr int kStreamThreads = (kConsumerWarps + 1) * 32;
+constexpr int kRingBytes = 96 * 1024;
+constexpr int kMaxSlots = 16;
+constexpr int kMaxRpc = 4;
+constexpr int kUnitsPerLane = 4;
+constexpr int kSegUnits = 32 * kUnitsPerLane;  // 16-byte units per row segment (2048 values)
+constexpr int kMaxSegs = 4;
+constexpr int kStreamMaxK = kMaxSegs * kSegUnits * 16;
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+__device__ unsigned int g_gemv_fault;
+
+__host__ __device__ constexpr int64_t round16(int64_t v) { return (v + 15) / 16 * 16; }
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    if (ok) return true;
+  }
+  atomicOr(&g_gemv_fault, 2u);
+  return false;
+}
+
+__global__ void __launch_bounds__(kStreamThreads, 2)
+gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, const float* __restrict__ x,
+                        float* __restrict__ y, int rpc, int slots) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int nb = K >> 5;
+  const int nunits = K >> 4;  // 16-byte units per row; unit u is half of block u / 2
+  const int nseg = (nunits + kSegUnits - 1) / kSegUnits;  // warps per row
+  const int ngroups = kConsumerWarps / nseg;               // rows in flight
+  const int r0 = (int)(((int64_t)N * blockIdx.x) / gridDim.x);
+  const int r1 = (int)(((int64_t)N * (blockIdx.x + 1)) / gridDim.x);
+  const int nchunks = (r1 - r0 + rpc - 1) / rpc;
+  const size_t chunk_bytes = (size_t)rpc * S;
+  // [ring | qx: K int8 | dx: nb f32 | part: [slot][row][seg] f32 | cnt: [slot][row] |
+  //  full, empty: kMaxSlots mbarriers each], every region on 16 bytes
+  uint8_t* ring = smem;
+  int8_t* qx = reinterpret_cast<int8_t*>(smem + kRingBytes);
+  float* dx = reinterpret_cast<float*>(smem + kRingBytes + round16(K));
+  float* part = reinterpret_cast<float*>(smem + kRingBytes + round16(K) + round16(4 * nb));
+  int* cnt = reinterpret_cast<int*>(part + kMaxSlots * kMaxRpc * kMaxSegs);
+  uint64_t* full = reinterpret_cast<uint64_t*>(cnt + kMaxSlots * kMaxRpc);
+  uint64_t* empty = full + kMaxSlots;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < slots; ++i) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&full[i])), "r"(1) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&empty[i])), "r"(rpc * nseg)
+                   : "memory");
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  for (int i = threadIdx.x; i < kMaxSlots * kMaxRpc; i += kStreamThreads) cnt[i] = 0;
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int j = 0; j < nchunks; ++j) {
+        const int slot = j % slots;
+        if (j >= slots && !bar_wait(&empty[slot], (uint32_t)((j / slots - 1) & 1))) break;
+        const int row = r0 + j * rpc;
+        const uint32_t bytes = (uint32_t)(min(rpc, r1 - row) * S);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&full[slot])),
+                     "r"(bytes) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     ::"r"(smem_u32(ring + (size_t)slot * chunk_bytes)), "l"(W + (size_t)row * S), "r"(bytes),
+                     "r"(smem_u32(&full[slot]))
+                     : "memory");
+        issued = j + 1;
+      }
+      // the copies must land before the CTA's shared memory is released
+      for (int j = (issued > slots ? issued - slots : 0); j < issued; ++j)
+        bar_wait(&full[j % slots], (uint32_t)((j / slots) & 1));
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  pdl_wait();
+  {
+    // float4 pieces of x, 8 lanes per block; the loads of up to four passes are issued
+    // together so K <= 8192 costs one L2 round trip
+    constexpr int kT = kConsumerWarps * 32;
+    constexpr int kQG = 4;
+    const int nquads = nb * 8;
+    float4 v[kQG];
+#pragma unroll
+    for (int g = 0; g < kQG; ++g) {
+      const int i = g * kT + threadIdx.x;
+      v[g] = i < nquads ? __ldg(reinterpret_cast<const float4*>(x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int g = 0; g < kQG; ++g) {
+      if (g * kT < nquads) {  // uniform across the warps: every lane shuffles
+        const int i = g * kT + threadIdx.x;
+        __half dh;
+        const int q = quantize_octet(v[g], dh);
+        if (i < nquads) {
+          reinterpret_cast<int*>(qx)[i] = q;
+          if ((i & 7) == 0) dx[i >> 3] = __half2float(dh);
+        }
+      }
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");  // consumer warps only
+
+  const int seg = warp % nseg, grp = warp / nseg;
+  if (grp >= ngroups) return;  // K = 6144: one warp of the sixteen has no segment
+  int4 xr[kUnitsPerLane];
+  float dxr[kUnitsPerLane];
+#pragma unroll
+  for (int t = 0; t < kUnitsPerLane; ++t) {
+    const int u = seg * kSegUnits + 32 * t + lane;
+    xr[t] = u < nunits ? *reinterpret_cast<const int4*>(qx + (size_t)u * 16) : make_int4(0, 0, 0, 0);
+    dxr[t] = u < nunits ? dx[u >> 1] : 0.0f;
+  }
+
+  for (int rr = grp; rr < r1 - r0; rr += ngroups) {
+    const int j = rr / rpc, ri = rr % rpc;
+    const int slot = j % slots;
+    if (!bar_wait(&full[slot], (uint32_t)((j / slots) & 1))) break;
+    const uint8_t* wrow = ring + (size_t)slot * chunk_bytes + (size_t)ri * S;
+    const __half* wsc = reinterpret_cast<const __half*>(wrow + K);
+    int4 wv[kUnitsPerLane];
+#pragma unroll
+    for (int t = 0; t < kUnitsPerLane; ++t) {
+      const int u = seg * kSegUnits + 32 * t + lane;
+      wv[t] = u < nunits ? *reinterpret_cast<const int4*>(wrow + (size_t)u * 16) : make_int4(0, 0, 0, 0);
+    }
+    int is[kUnitsPerLane];
+#pragma unroll
+    for (int t = 0; t < kUnitsPerLane; ++t) is[t] = dot16(wv[t], xr[t], 0);
+#pragma unroll
+    for (int t = 0; t < kUnitsPerLane; ++t) is[t] += __shfl_xor_sync(kFull, is[t], 1);
+    float acc[kUnitsPerLane];
+#pragma unroll
+    for (int t = 0; t < kUnitsPerLane; ++t) {
+      const int u = seg * kSegUnits + 32 * t + lane;
+      acc[t] = 0.0f;
+      if (u < nunits && !(lane & 1))  // pairs (2p, 2p + 1) are valid together: nunits is even
+        acc[t] = __fmul_rn(__fmul_rn(__int2float_rn(is[t]), __half2float(wsc[u >> 1])), dxr[t]);
+    }
+    const float accs = warp_sum((acc[0] + acc[1]) + (acc[2] + acc[3]));
+    __syncwarp();
+    if (lane == 0) {
+      if (nseg == 1) {
+        y[r0 + rr] = accs;
+      } else {
+        float* pr = part + (slot * kMaxRpc + ri) * kMaxSegs;
+        pr[seg] = accs;
+        __threadfence_block();
+        if (atomicAdd(&cnt[slot * kMaxRpc + ri], 1) == nseg - 1) {
+          __threadfence_block();
+          float sum = pr[0];
+          for (int q = 1; q < nseg; ++q) sum += pr[q];
+          y[r0 + rr] = sum;
+          cnt[slot * kMaxRpc + ri] = 0;
+        }
+      }
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[slot])) : "memory");
+    }
+  }
+}
+
+// Rows per chunk and ring slots of the M = 1 streaming kernel for this K (slots 0: the
+// kernel does not apply).  Chunks shrink until at least 8 fit in the ring.
+void stream_plan(int64_t k, int64_t S, int* rpc, int* slots) {
+  *rpc = kMaxRpc;
+  *slots = 0;
+  if (k > kStreamMaxK) return;
+  while (*rpc > 1 && kRingBytes / (*rpc * S) < 8) *rpc /= 2;
+  const int64_t s = kRingBytes / (*rpc * S);
+  *slots = s < 2 ? 0 : (int)(s > kMaxSlots ? kMaxSlots : s);
+}
+
+size_t stream_smem_bytes(int64_t k) {
+  return (size_t)(kRingBytes + round16(k) + round16(4 * (k / kQK)) + kMaxSlots * kMaxRpc * kMaxSegs * 4 +
+                  kMaxSlots * kMaxRpc * 4 + 2 * kMaxSlots * 8);
+}
+
+cudaError_t launch_stream(const q8lin_weight& w, const float* x, float* y, int rpc, int slots, cudaStream_t s) {
+  const int K = (int)w.k, N = (int)w.n;
+  const size_t smem = stream_smem_bytes(K);
+  static int configured_smem[128] = {0};
+  const int dev = (w.device >= 0 && w.device < 128) ? w.device : 0;
+  if ((int)smem > configured_smem[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_q8_0_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    // the largest shared-memory carveout, so that two CTAs (this launch's and the
+    // next one's) fit on an SM
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_q8_0_stream_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               (int)cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    configured_smem[dev] = (int)smem;
+  }
+  int grid = sm_count(w.device);
+  if (grid > N) grid = N;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kStreamThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_q8_0_stream_kernel, (const uint8_t*)w.packed, w.row_stride, N, K, x, y, rpc,
+                            slots);
+}
+
 template <int M>
 cudaError_t launch_m(const q8lin_weight& w, const float* x, float* y, cudaStream_t s) {
   const int K = (int)w.k, N = (int)w.n;
@@ -190,7 +442,21 @@ size_t gemv_smem_bytes(int m, int64_t k) {
   return (((size_t)m * k + 15) / 16) * 16 + (size_t)m * (k / kQK) * sizeof(float);
 }
 
+cudaError_t read_gemv_fault(unsigned int* flags, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(flags, g_gemv_fault, sizeof(unsigned int));
+  if (e == cudaSuccess && clear) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_gemv_fault, &z, sizeof(z));
+  }
+  return e;
+}
+
 cudaError_t launch_gemv(const q8lin_weight& w, const float* x, float* y, int m, cudaStream_t s) {
+  if (m == 1) {
+    int rpc, slots;
+    stream_plan(w.k, w.row_stride, &rpc, &slots);
+    if (slots > 0) return launch_stream(w, x, y, rpc, slots, s);
+  }
   switch (m) {
     case 1: return launch_m<1>(w, x, y, s);
     case 2: return launch_m<2>(w, x, y, s);

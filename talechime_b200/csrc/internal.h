@@ -48,6 +48,8 @@ size_t gemm_tc_workspace_bytes(int64_t m, int64_t k);
 cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
                            cudaStream_t s);
 cudaError_t read_tc_fault(unsigned int* flags, bool clear);
+// M = 1 streaming GEMV (gemv.cu): bit 1 of the fault word.
+cudaError_t read_gemv_fault(unsigned int* flags, bool clear);
 
 int sm_count(int device);
 
