@@ -135,6 +135,18 @@ int q8lin_fault_status(int device, uint32_t* flags, int clear);
 int q8lin_quantize_rows(const float* x, int64_t m, int64_t k, int8_t* qs, uint16_t* d_f16,
                         q8lin_stream_t stream);
 
+/*
+ * SwiGLU between the gate/up and down projections of the MLP: gu is the f32 output
+ * [M][2*inter] of one fused gate+up linear (gate columns first, then up), h[M][inter] =
+ * silu(gate) * up with candle's f32 silu v / (1 + exp(-v)).  Replaces the
+ * `l.gate.forward(&h)?.silu()? * l.up.forward(&h)?` step of
+ * crates/voxcpm/src/transformer.rs:147-150 (two linears, silu, mul) when the gate and
+ * up weights are stored as one fused weight, as the tensor-parallel shards are.
+ * gu and h are device pointers (4-byte aligned; 16-byte aligned rows take the
+ * vectorized kernel).  Capture-safe.
+ */
+int q8lin_swiglu(const float* gu, int64_t m, int64_t inter, float* h, q8lin_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

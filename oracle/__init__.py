@@ -51,6 +51,8 @@ def lib() -> ctypes.CDLL:
         L.q8o_matmul.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
                                  ctypes.c_int64, ctypes.c_void_p, ctypes.c_int]
         L.q8o_matmul.restype = ctypes.c_int
+        L.q8o_swiglu.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]
+        L.q8o_swiglu.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -111,6 +113,28 @@ def matmul(x: np.ndarray, w_blocks: np.ndarray, n: int, threads: int = 1) -> np.
     if rc != 0:
         raise ValueError(f"oracle matmul failed with status {rc}")
     return y
+
+
+def swiglu(gu: np.ndarray) -> np.ndarray:
+    """silu(gate) * up over gu f32 [M, 2I] (gate columns first) -> h f32 [M, I]."""
+    gu = np.ascontiguousarray(gu, dtype=np.float32)
+    m, two_i = gu.shape
+    if two_i % 2:
+        raise ValueError("gu must have an even number of columns")
+    h = np.empty((m, two_i // 2), dtype=np.float32)
+    rc = lib().q8o_swiglu(_ptr(gu), m, two_i // 2, _ptr(h))
+    if rc != 0:
+        raise ValueError(f"oracle swiglu failed with status {rc}")
+    return h
+
+
+def mlp(x: np.ndarray, gate: np.ndarray, up: np.ndarray, down: np.ndarray, hidden: int, inter: int,
+        threads: int = 1) -> np.ndarray:
+    """The VoxCPM MLP on the CPU path: down(silu(gate(x)) * up(x)), three candle
+    QMatMul::forward calls (crates/voxcpm/src/transformer.rs:147-150)."""
+    g = matmul(x, gate, inter, threads)
+    u = matmul(x, up, inter, threads)
+    return matmul(swiglu(np.concatenate([g, u], axis=1)), down, hidden, threads)
 
 
 def f32_to_f16_bits(v: float) -> int:

@@ -248,3 +248,24 @@ int q8o_matmul(const float* x, int64_t m, int64_t k, const uint8_t* w, int64_t n
   free(qx); free(dh); free(dx); free(jobs); free(tids);
   return 0;
 }
+
+/*
+ * SwiGLU of the VoxCPM MLP (crates/voxcpm/src/transformer.rs:147-150:
+ * `l.down.forward(&(l.gate.forward(&h)?.silu()? * l.up.forward(&h)?)?)`).
+ * candle-core's f32 silu unary op is v / (1 + exp(-v)), each operation rounded to f32
+ * (exp from the platform libm, as Rust's f32::exp), then the product with up.
+ * gu[m][2*inter]: gate columns [0, inter), up columns [inter, 2*inter).
+ */
+int q8o_swiglu(const float* gu, int64_t m, int64_t inter, float* h) {
+  if (m < 0 || inter <= 0) return 1;
+  for (int64_t r = 0; r < m; ++r) {
+    const float* g = gu + r * 2 * inter;
+    const float* u = g + inter;
+    for (int64_t i = 0; i < inter; ++i) {
+      const float e = expf(-g[i]);
+      const float s = g[i] / (1.0f + e);
+      h[r * inter + i] = s * u[i];
+    }
+  }
+  return 0;
+}

@@ -44,6 +44,7 @@ SIGNATURES = {
     "q8lin_quantize_rows": (ctypes.c_int, [_c_p, _i64, _i64, _c_p, _c_p, _c_p]),
     "q8lin_forward_noalloc": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p]),
     "q8lin_fault_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
+    "q8lin_swiglu": (ctypes.c_int, [_c_p, _i64, _i64, _c_p, _c_p]),
 }
 
 _lock = threading.Lock()

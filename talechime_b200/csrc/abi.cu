@@ -358,4 +358,15 @@ int q8lin_quantize_rows(const float* x, int64_t m, int64_t k, int8_t* qs, uint16
   return Q8LIN_OK;
 }
 
+int q8lin_swiglu(const float* gu, int64_t m, int64_t inter, float* h, q8lin_stream_t stream) {
+  if (m < 0 || inter <= 0) return fail(Q8LIN_ERR_SHAPE, "swiglu needs m >= 0 and inter > 0");
+  if (m == 0) return Q8LIN_OK;
+  if (!gu || !h) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "gu and h must be non-null device pointers");
+  if ((reinterpret_cast<uintptr_t>(gu) & 3u) || (reinterpret_cast<uintptr_t>(h) & 3u))
+    return fail(Q8LIN_ERR_ALIGNMENT, "gu and h must be 4-byte aligned");
+  cudaError_t e = launch_swiglu(gu, m, inter, h, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "swiglu launch");
+  return Q8LIN_OK;
+}
+
 }  // extern "C"

@@ -167,7 +167,7 @@ gemv_q8_0_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K,
 // two CTAs fit on an SM -- the CTA of the next linear in the stream is resident while
 // this one runs.  The CTA's rows are one contiguous byte range of the packed plane,
 // copied into a shared-memory ring of `rpc`-row chunks with 1-D bulk copies
-// (cp.async.bulk, no multicast).
+// (cp.async.bulk from this GPU's own memory).
 //
 // Order of events:
 //   1. launch_dependents at once: the next linear's CTAs may become resident and start

@@ -51,6 +51,9 @@ cudaError_t read_tc_fault(unsigned int* flags, bool clear);
 // M = 1 streaming GEMV (gemv.cu): bit 1 of the fault word.
 cudaError_t read_gemv_fault(unsigned int* flags, bool clear);
 
+// SwiGLU between the MLP projections (mlp.cu): h[m][i] = silu(gu[m][i]) * gu[m][inter + i].
+cudaError_t launch_swiglu(const float* gu, int64_t m, int64_t inter, float* h, cudaStream_t s);
+
 int sm_count(int device);
 
 // Programmatic dependent launch on/off (env Q8LIN_PDL=0 turns it off; read once).

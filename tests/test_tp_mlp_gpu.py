@@ -1,0 +1,112 @@
+"""SwiGLU kernel and the (tensor-parallel) Q8_0 MLP on the GPU against the oracle."""
+import ctypes
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+
+from talechime_b200 import _lib, synth
+from talechime_b200.tp_mlp import SwiGLUMLP
+from tests.conftest import assert_close_to_oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def _weights(seed, hidden, inter, m):
+    rng = np.random.default_rng(seed)
+    gate = synth.q8_0_blocks(rng, inter, hidden)
+    up = synth.q8_0_blocks(rng, inter, hidden)
+    down = synth.q8_0_blocks(rng, hidden, inter)
+    x = rng.standard_normal((m, hidden)).astype(np.float32)
+    return x, gate, up, down
+
+
+@pytest.mark.parametrize("m,inter", [(3, 256), (2, 30), (5, 4096)])
+def test_swiglu_kernel_matches_oracle(oracle_lib, cuda_device, m, inter):
+    rng = np.random.default_rng(100 + inter)
+    gu = (rng.standard_normal((m, 2 * inter)) * 3).astype(np.float32)
+    ref = oracle_lib.swiglu(gu)
+    g = torch.from_numpy(gu).to(cuda_device)
+    h = torch.empty((m, inter), device=cuda_device)
+    _lib.check(_lib.lib().q8lin_swiglu(ctypes.c_void_p(g.data_ptr()), m, inter, ctypes.c_void_p(h.data_ptr()),
+                                       ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    got = h.cpu().numpy()
+    # expf differs from the CPU libm exp by a few ulp: elementwise relative bound
+    assert np.all(np.abs(got - ref) <= 4e-7 * np.abs(ref) + 1e-30)
+
+
+def test_swiglu_rejects_bad_arguments(cuda_device):
+    L = _lib.lib()
+    assert L.q8lin_swiglu(None, 1, 4, None, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.q8lin_swiglu(None, -1, 4, None, None) == _lib.ERR_SHAPE
+
+
+@pytest.mark.parametrize("m", [1, 5, 40])
+def test_mlp_single_gpu_matches_oracle(oracle_lib, cuda_device, m):
+    hidden, inter = 512, 1024
+    x, gate, up, down = _weights(200 + m, hidden, inter, m)
+    ref = oracle_lib.mlp(x, gate, up, down, hidden, inter, threads=16)
+    mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device)
+    y = mlp.forward(torch.from_numpy(x).to(cuda_device))
+    assert_close_to_oracle(y.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_partials_sum_to_oracle(oracle_lib, cuda_device, world):
+    """Every rank's shard on one GPU; the host adds the partials (the all-reduce)."""
+    hidden, inter, m = 512, 2048, 4
+    x, gate, up, down = _weights(300 + world, hidden, inter, m)
+    ref = oracle_lib.mlp(x, gate, up, down, hidden, inter, threads=16)
+    xt = torch.from_numpy(x).to(cuda_device)
+    total = torch.zeros((m, hidden), device=cuda_device)
+    for r in range(world):
+        part = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device, rank=r, world=world)
+        total += part.partial(xt)
+    assert_close_to_oracle(total.cpu().numpy(), ref)
+
+
+def test_tp_forward_without_process_group_fails_loudly(cuda_device):
+    hidden, inter = 256, 512
+    x, gate, up, down = _weights(400, hidden, inter, 1)
+    part = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device, rank=0, world=2)
+    with pytest.raises(_lib.Q8LinError):
+        part.forward(torch.from_numpy(x).to(cuda_device))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_rank(rank, world, port, result_dir):
+    torch.cuda.set_device(rank)
+    torch.distributed.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                         world_size=world, timeout=timedelta(seconds=60),
+                                         device_id=torch.device("cuda", rank))
+    try:
+        hidden, inter, m = 1024, 2048, 3
+        x, gate, up, down = _weights(500, hidden, inter, m)
+        dev = torch.device("cuda", rank)
+        mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, rank=rank, world=world)
+        y = mlp.forward(torch.from_numpy(x).to(dev))
+        torch.cuda.synchronize(dev)
+        np.save(os.path.join(result_dir, f"y{rank}.npy"), y.cpu().numpy())
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp_nccl_two_gpus(oracle_lib, cuda_device, tmp_path):
+    world = 2
+    port = _free_port()
+    torch.multiprocessing.start_processes(_nccl_rank, args=(world, port, str(tmp_path)), nprocs=world,
+                                          join=True, start_method="spawn")
+    x, gate, up, down = _weights(500, 1024, 2048, 3)
+    ref = oracle_lib.mlp(x, gate, up, down, 1024, 2048, threads=16)
+    y0, y1 = np.load(tmp_path / "y0.npy"), np.load(tmp_path / "y1.npy")
+    assert np.array_equal(y0, y1)
+    assert_close_to_oracle(y0, ref)
