@@ -273,6 +273,60 @@ def run_sweep(torch, L, dev, stream) -> list:
     return out
 
 
+def run_tp_mlp(torch, dist, dev, rank: int, world: int, reps: int = 20) -> dict:
+    """Config 4: the Q8_0 SwiGLU MLP at hidden 4096 / intermediate 14336 split over the
+    `world` ranks (gate/up by output rows, down by input blocks, one NCCL all-reduce per
+    forward; talechime_b200/tp_mlp.py).  Device time per forward with CUDA events, max
+    over ranks; every rank runs the same launches and collectives."""
+    from talechime_b200.tp_mlp import SwiGLUMLP
+
+    hidden, inter = 4096, 14336
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4242)  # identical full weights on every rank; each keeps its shards
+
+    def blocks(n, k):
+        nb = k // 32
+        b = torch.empty((n, nb, 34), dtype=torch.uint8, device=dev)
+        b[:, :, 2:] = torch.randint(-127, 128, (n, nb, 32), generator=gen, device=dev,
+                                    dtype=torch.int8).view(torch.uint8)
+        d = (torch.randn((n, nb), generator=gen, device=dev).abs() * (0.02 / 127.0)).half()
+        b[:, :, :2] = d.view(torch.uint8).view(n, nb, 2)
+        return b
+
+    gate, up, down = blocks(inter, hidden), blocks(inter, hidden), blocks(hidden, inter)
+    mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, rank=rank, world=world)
+    del gate, up, down
+    torch.cuda.synchronize(dev)
+    weight_bytes = 3 * inter * hidden * 34 // 32
+    out = {"config": f"SwiGLU MLP hidden {hidden} / intermediate {inter}, Q8_0, gate+up column-split, "
+                     f"down row-split over {world} GPU(s), NCCL all-reduce", "weight_bytes": weight_bytes,
+           "per_m": []}
+    for m in (1, 16, 256):
+        x = torch.randn((m, hidden), generator=gen, device=dev)
+        for _ in range(3):
+            mlp.forward(x)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = reps if m < 256 else max(3, reps // 2)
+        e0.record()
+        for _ in range(n):
+            mlp.forward(x)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / n
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        out["per_m"].append({"m": m, "ms": ms, "weight_tb_s": weight_bytes / (ms * 1e-3) / 1e12,
+                             "tokens_per_s": m / (ms * 1e-3), "tflops": 2.0 * 3 * inter * hidden * m / (ms * 1e-3) / 1e12})
+    del mlp
+    torch.cuda.synchronize(dev)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -282,6 +336,7 @@ def main() -> None:
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds for the cpu_baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    ap.add_argument("--no-tp-mlp", action="store_true", help="skip the tensor-parallel MLP measurement")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layer copies (28 = the benchmark; fewer only for small profiling captures)")
     ap.add_argument("--case", default=None,
@@ -452,7 +507,7 @@ def main() -> None:
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                      "frac": achieved_gbs / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                      if peak_kind == "measured" else "fallback 6.65 TB/s",
-                     "traffic": traffic, "kernel": "gemv_q8_0_kernel<1>",
+                     "traffic": traffic, "kernel": "gemv_q8_0_stream_kernel",
                      "bytes_per_launch": bytes_per_step / launches_per_step},
         "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms, "steps": e2e_steps,
@@ -467,6 +522,8 @@ def main() -> None:
             "value": v, "unit": "TB/s", "cores": threads, "kind": "port",
             "sample": f"{done} projections (qkv/o/gate_up/down of 2 layers, M=1) in {el:.1f} s with the "
                       f"candle-CPU restatement (oracle/q8_0_oracle.c)"}
+    if not args.no_tp_mlp:
+        line["tp_mlp"] = run_tp_mlp(torch, dist, dev, rank, world)
     if args.sweep and rank == 0:
         line["sweep"] = run_sweep(torch, L, dev, stream)
     if rank == 0:
