@@ -81,8 +81,10 @@ int q8lin_weight_dequantize(const q8lin_weight* w, float* out, q8lin_stream_t st
 /* Write the weight back in GGUF block layout (device memory, N*K/32*34 bytes). */
 int q8lin_weight_export_gguf(const q8lin_weight* w, void* out_blocks, q8lin_stream_t stream);
 
-/* Workspace bytes q8lin_forward_ws needs for M rows (0 for M <= 16): the activations as
- * f16 integers [M][K] plus transposed f32 scales [K/32][M], each 256-byte aligned. */
+/* Workspace bytes q8lin_forward_ws needs for M rows: 0 for M <= 4 (decode GEMV); for
+ * 5 <= M <= 32 the int8 activations [M][K], transposed f32 scales and the split-K
+ * partial sums of the int8 tensor-core path; for larger M the activations as f16
+ * integers [M][K] plus transposed f32 scales.  Regions are 256-byte aligned. */
 size_t q8lin_workspace_size(const q8lin_weight* w, int64_t m);
 
 /*
@@ -120,8 +122,8 @@ int q8lin_forward_noalloc(const q8lin_weight* w, const float* x, float* y, int64
 
 /*
  * Device-side fault word of `device` (bit 0: a tensor-core kernel's bounded wait ran
- * out, bit 1: the M = 1 streaming GEMV's bounded wait ran out; the kernel returned
- * early and its output is invalid).  Reads it with a
+ * out, bit 1: the M = 1 streaming GEMV's, bit 2: the small-batch int8 kernel's; the
+ * kernel returned early and its output is invalid).  Reads it with a
  * device synchronisation; `clear` resets it.  No counterpart in the reference (candle's
  * kernels have no bounded waits); this is the library's failure-detection hook.
  */

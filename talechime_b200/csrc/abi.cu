@@ -52,12 +52,19 @@ constexpr size_t kAlign = 256;
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Dispatch by activation rows (crossovers measured on B200 in CUDA graphs): M <= 4
+// streams the weights through the GEMV kernels; 5 <= M <= 32 takes the int8
+// tensor-core path with the weights on the MMA's 128-row side; larger batches the f16
+// tensor-core GEMM.
+constexpr int kGemvPathMaxM = 4;
 bool use_gemv(int64_t m, int64_t k) {
-  return m >= 1 && m <= kGemvMaxM && gemv_smem_bytes((int)m, k) <= kGemvSmemLimit;
+  return m >= 1 && m <= kGemvPathMaxM && gemv_smem_bytes((int)m, k) <= kGemvSmemLimit;
 }
+bool use_skinny(int64_t m) { return m > kGemvPathMaxM && m <= kSkinnyMaxM; }
 
 size_t workspace_bytes(int64_t m, int64_t k) {
   if (m <= 0 || use_gemv(m, k)) return 0;
+  if (use_skinny(m)) return gemm_skinny_workspace_bytes(m, k);
   return gemm_tc_workspace_bytes(m, k);
 }
 
@@ -304,6 +311,11 @@ int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
                                          std::to_string(need) + " bytes needed for M=" + std::to_string(m));
   if (reinterpret_cast<uintptr_t>(workspace) % kAlign)
     return fail(Q8LIN_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  if (use_skinny(m)) {
+    e = launch_gemm_skinny(*w, x, workspace, y, m, s);
+    if (e != cudaSuccess) return cuda_fail(e, "int8 tensor-core matmul launch");
+    return Q8LIN_OK;
+  }
   e = launch_gemm_tc(*w, x, workspace, y, m, s);
   if (e != cudaSuccess) return cuda_fail(e, "tensor-core gemm launch");
   return Q8LIN_OK;
@@ -338,11 +350,12 @@ int q8lin_fault_status(int device, uint32_t* flags, int clear) {
   int st = check_device(device);
   if (st != Q8LIN_OK) return st;
   DeviceGuard guard(device);
-  unsigned int f = 0, g = 0;
+  unsigned int f = 0, g = 0, h = 0;
   cudaError_t e = read_tc_fault(&f, clear != 0);
   if (e == cudaSuccess) e = read_gemv_fault(&g, clear != 0);
+  if (e == cudaSuccess) e = read_skinny_fault(&h, clear != 0);
   if (e != cudaSuccess) return cuda_fail(e, "read fault word");
-  *flags = f | g;
+  *flags = f | g | h;
   return Q8LIN_OK;
 }
 

@@ -48,6 +48,15 @@ size_t gemm_tc_workspace_bytes(int64_t m, int64_t k);
 cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
                            cudaStream_t s);
 cudaError_t read_tc_fault(unsigned int* flags, bool clear);
+
+// Small-batch int8 tensor-core path (gemm_skinny.cu), for m up to kSkinnyMaxM: quantize
+// x to int8 + transposed scales in `workspace`, then the kind::i8 matmul (split-K with
+// partial sums in the workspace).  Fault word bit 2.
+constexpr int kSkinnyMaxM = 32;
+size_t gemm_skinny_workspace_bytes(int64_t m, int64_t k);
+cudaError_t launch_gemm_skinny(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
+                               cudaStream_t s);
+cudaError_t read_skinny_fault(unsigned int* flags, bool clear);
 // M = 1 streaming GEMV (gemv.cu): bit 1 of the fault word.
 cudaError_t read_gemv_fault(unsigned int* flags, bool clear);
 

@@ -75,6 +75,17 @@ def fuse_rows(a, b):
     return np.ascontiguousarray(np.concatenate([a, b], axis=0))
 
 
+def swiglu(gu: torch.Tensor, inter: int) -> torch.Tensor:
+    """h[..., inter] = silu(gu[..., :inter]) * gu[..., inter:] on the device (q8lin_swiglu)."""
+    if gu.shape[-1] != 2 * inter or gu.dtype != torch.float32 or not gu.is_contiguous() or not gu.is_cuda:
+        raise Q8LinError(_lib.ERR_SHAPE, f"gu {tuple(gu.shape)} is not a contiguous f32 CUDA [..., {2 * inter}]")
+    m = gu.numel() // (2 * inter)
+    h = torch.empty(gu.shape[:-1] + (inter,), dtype=torch.float32, device=gu.device)
+    check(_lib.lib().q8lin_swiglu(ctypes.c_void_p(gu.data_ptr()), m, inter, ctypes.c_void_p(h.data_ptr()),
+                                  ctypes.c_void_p(_stream_ptr(gu.device))))
+    return h
+
+
 class SwiGLUMLP:
     """One rank's share of ``down(silu(gate(x)) * up(x))`` (all of it when world = 1)."""
 
@@ -106,12 +117,7 @@ class SwiGLUMLP:
 
     def partial(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """This rank's contribution to y (before the all-reduce)."""
-        gu = self.gate_up.forward(x)
-        m = gu.numel() // (2 * self.inter_local)
-        h = torch.empty(gu.shape[:-1] + (self.inter_local,), dtype=torch.float32, device=self.device)
-        check(_lib.lib().q8lin_swiglu(ctypes.c_void_p(gu.data_ptr()), m, self.inter_local,
-                                      ctypes.c_void_p(h.data_ptr()), ctypes.c_void_p(_stream_ptr(self.device))))
-        return self.down.forward(h, out=out)
+        return self.down.forward(swiglu(self.gate_up.forward(x), self.inter_local), out=out)
 
     def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self.world > 1 and not (torch.distributed.is_available() and torch.distributed.is_initialized()):

@@ -9,10 +9,40 @@ import pytest
 import torch
 
 from talechime_b200 import _lib, synth
-from talechime_b200.tp_mlp import SwiGLUMLP
+from talechime_b200.tp_mlp import SwiGLUMLP, shard_k, shard_rows, swiglu
 from tests.conftest import assert_close_to_oracle
 
 pytestmark = pytest.mark.gpu
+
+# End to end, the down projection re-quantizes h: a last-bit difference in the gate/up
+# output (tree and split-K summation orders) can move an h value across a Q8_0 rounding
+# boundary, a change of one quantization step d in that element.  Each projection is
+# held to the per-linear tolerance against the oracle fed with the same input; the whole
+# MLP against the all-oracle MLP gets this looser bound.
+MLP_E2E_REL_L2 = 1e-3
+
+
+def _check_stages(oracle_lib, mlp, x_np, gate, up, down, hidden, inter, rank=0, world=1):
+    """gate/up, SwiGLU and down of one rank, each against the oracle on the same input."""
+    il = inter // world
+    xt = torch.from_numpy(x_np).to(mlp.device)
+    gu = mlp.gate_up.forward(xt)
+    gu_ref = np.concatenate([oracle_lib.matmul(x_np, shard_rows(gate, inter, hidden, rank, world), il, threads=16),
+                             oracle_lib.matmul(x_np, shard_rows(up, inter, hidden, rank, world), il, threads=16)],
+                            axis=1)
+    assert_close_to_oracle(gu.cpu().numpy(), gu_ref)
+    h = swiglu(gu, il)
+    h_np = h.cpu().numpy()
+    h_ref = oracle_lib.swiglu(gu.cpu().numpy())
+    assert np.all(np.abs(h_np - h_ref) <= 4e-7 * np.abs(h_ref) + 1e-30)
+    part = mlp.down.forward(h).cpu().numpy()
+    part_ref = oracle_lib.matmul(h_np, shard_k(down, hidden, inter, rank, world), hidden, threads=16)
+    assert_close_to_oracle(part, part_ref)
+    return part
+
+
+def _rel_l2(y, ref):
+    return float(np.linalg.norm(y.astype(np.float64) - ref) / np.linalg.norm(ref))
 
 
 def _weights(seed, hidden, inter, m):
@@ -44,14 +74,16 @@ def test_swiglu_rejects_bad_arguments(cuda_device):
     assert L.q8lin_swiglu(None, -1, 4, None, None) == _lib.ERR_SHAPE
 
 
-@pytest.mark.parametrize("m", [1, 5, 40])
+@pytest.mark.parametrize("m", [1, 5, 40, 100])
 def test_mlp_single_gpu_matches_oracle(oracle_lib, cuda_device, m):
     hidden, inter = 512, 1024
     x, gate, up, down = _weights(200 + m, hidden, inter, m)
-    ref = oracle_lib.mlp(x, gate, up, down, hidden, inter, threads=16)
     mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device)
-    y = mlp.forward(torch.from_numpy(x).to(cuda_device))
-    assert_close_to_oracle(y.cpu().numpy(), ref)
+    part = _check_stages(oracle_lib, mlp, x, gate, up, down, hidden, inter)
+    y = mlp.forward(torch.from_numpy(x).to(cuda_device)).cpu().numpy()
+    assert np.array_equal(y, part)  # forward() is the three stages
+    ref = oracle_lib.mlp(x, gate, up, down, hidden, inter, threads=16)
+    assert _rel_l2(y, ref) <= MLP_E2E_REL_L2
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
@@ -59,13 +91,19 @@ def test_tp_partials_sum_to_oracle(oracle_lib, cuda_device, world):
     """Every rank's shard on one GPU; the host adds the partials (the all-reduce)."""
     hidden, inter, m = 512, 2048, 4
     x, gate, up, down = _weights(300 + world, hidden, inter, m)
-    ref = oracle_lib.mlp(x, gate, up, down, hidden, inter, threads=16)
+    total = np.zeros((m, hidden), dtype=np.float64)
+    total_ref = np.zeros((m, hidden), dtype=np.float64)
     xt = torch.from_numpy(x).to(cuda_device)
-    total = torch.zeros((m, hidden), device=cuda_device)
     for r in range(world):
         part = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device, rank=r, world=world)
-        total += part.partial(xt)
-    assert_close_to_oracle(total.cpu().numpy(), ref)
+        p = _check_stages(oracle_lib, part, x, gate, up, down, hidden, inter, rank=r, world=world)
+        assert np.array_equal(part.partial(xt).cpu().numpy(), p)
+        total += p
+        h = swiglu(part.gate_up.forward(xt), inter // world).cpu().numpy()
+        total_ref += oracle_lib.matmul(h, shard_k(down, hidden, inter, r, world), hidden, threads=16)
+    assert_close_to_oracle(total, total_ref)
+    ref = oracle_lib.mlp(x, gate, up, down, hidden, inter, threads=16)
+    assert _rel_l2(total, ref) <= MLP_E2E_REL_L2
 
 
 def test_tp_forward_without_process_group_fails_loudly(cuda_device):
@@ -109,4 +147,4 @@ def test_tp_nccl_two_gpus(oracle_lib, cuda_device, tmp_path):
     ref = oracle_lib.mlp(x, gate, up, down, 1024, 2048, threads=16)
     y0, y1 = np.load(tmp_path / "y0.npy"), np.load(tmp_path / "y1.npy")
     assert np.array_equal(y0, y1)
-    assert_close_to_oracle(y0, ref)
+    assert _rel_l2(y0, ref) <= MLP_E2E_REL_L2
