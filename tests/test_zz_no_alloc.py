@@ -41,6 +41,15 @@ def test_noalloc_matches_forward_on_two_calls(cuda_device):
         assert_close_to_oracle(y.cpu().numpy(), y_ref.cpu().numpy())
 
 
+def test_noalloc_is_bit_exact_with_the_cpu_path(oracle_lib, cuda_device):
+    """Its matmul adds the block terms in block order with candle's per-product rounding."""
+    x, w = synth.case(24, 9, 1024, 200)
+    q = QMatMul.from_gguf_blocks(w, 200, 1024, device=cuda_device)
+    y = _noalloc(q, torch.from_numpy(x).to(cuda_device), 9)
+    torch.cuda.synchronize()
+    assert np.array_equal(y.cpu().numpy(), oracle_lib.matmul(x, w, 200, threads=16))
+
+
 def test_noalloc_rejects_sizes_beyond_its_scratch(cuda_device):
     k, n = 2048, 64
     _, w = synth.case(23, 1, k, n)
