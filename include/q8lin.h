@@ -149,6 +149,38 @@ int q8lin_quantize_rows(const float* x, int64_t m, int64_t k, int8_t* qs, uint16
  */
 int q8lin_swiglu(const float* gu, int64_t m, int64_t inter, float* h, q8lin_stream_t stream);
 
+/*
+ * Decode-step building blocks around the linears (batch 1, f32, device pointers).  The
+ * position `pos` and tokens are device int32 values, so a captured CUDA graph of one
+ * step replays for every token: q8lin_argmax writes the next token and advances pos.
+ * Replace the per-layer tensor ops of crates/voxcpm/src/transformer.rs:107-155 and
+ * attention.rs:28-98 (rms_norm, rotate, KV-cache cat, grouped attention, residual add)
+ * and the greedy pick of the decode loop.
+ */
+/* Dequantized rows tokens[0..n) of a Q8_0 embedding weight [vocab][hidden] -> out[n][hidden]. */
+int q8lin_embed_rows(const q8lin_weight* w, const int32_t* tokens, int64_t n, float* out, q8lin_stream_t stream);
+/* y[m][n] = x / sqrt(sum(x^2)/n + eps) * weight (candle_nn::ops::rms_norm). */
+int q8lin_rmsnorm(const float* x, const float* weight, int64_t m, int64_t n, float eps, float* y,
+                  q8lin_stream_t stream);
+/* qkv[(hq + 2 hkv) * d] of the token at *pos: rotated q -> q_out[hq][d], rotated k and v
+ * -> k_cache / v_cache [hkv][max_t][d] at row *pos.  cos_t / sin_t: [max_t][d/2]. */
+int q8lin_rope_kv(const float* qkv, const int32_t* pos, const float* cos_t, const float* sin_t, float* k_cache,
+                  float* v_cache, int32_t hq, int32_t hkv, int32_t d, int32_t max_t, float* q_out,
+                  q8lin_stream_t stream);
+size_t q8lin_attention_workspace_size(int32_t hq, int32_t max_t);
+/* out[hq][d] = softmax(q k^T / sqrt(d)) v over cache rows [0, *pos], kv head = q head /
+ * (hq / hkv); d = 128.  The workspace must be zero-filled once before first use. */
+int q8lin_attention_decode(const float* q, const float* k_cache, const float* v_cache, const int32_t* pos,
+                           int32_t hq, int32_t hkv, int32_t d, int32_t max_t, void* workspace, size_t workspace_bytes,
+                           float* out, q8lin_stream_t stream);
+/* x[0..n) += y[0..n). */
+int q8lin_add(float* x, const float* y, int64_t n, q8lin_stream_t stream);
+size_t q8lin_argmax_workspace_size(void);
+/* *token = argmax(logits[0..n)) (lowest index on ties); if pos != NULL, *pos += 1.  The
+ * workspace must be zero-filled once before first use. */
+int q8lin_argmax(const float* logits, int64_t n, void* workspace, size_t workspace_bytes, int32_t* token, int32_t* pos,
+                 q8lin_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

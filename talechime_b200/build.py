@@ -19,7 +19,7 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libq8lin.so")
 OBJDIR = os.path.join(PKG, "_build")
 
-SOURCES = ["abi.cu", "layout.cu", "gemv.cu", "gemm_simt.cu", "gemm_tc.cu", "noalloc.cu", "mlp.cu", "gemm_skinny.cu"]
+SOURCES = ["abi.cu", "layout.cu", "gemv.cu", "gemm_simt.cu", "gemm_tc.cu", "noalloc.cu", "mlp.cu", "gemm_skinny.cu", "decoder.cu"]
 HEADERS = ["common.cuh", "internal.h"]
 
 NVCC_FLAGS = [

@@ -1,5 +1,6 @@
 // C ABI of libq8lin.so (declared in include/q8lin.h): argument checks, weight
 // upload/repack, workspace management and dispatch to the kernels.
+#include <climits>
 #include <cuda_runtime.h>
 #include <stdlib.h>
 
@@ -379,6 +380,87 @@ int q8lin_swiglu(const float* gu, int64_t m, int64_t inter, float* h, q8lin_stre
     return fail(Q8LIN_ERR_ALIGNMENT, "gu and h must be 4-byte aligned");
   cudaError_t e = launch_swiglu(gu, m, inter, h, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "swiglu launch");
+  return Q8LIN_OK;
+}
+
+int q8lin_embed_rows(const q8lin_weight* w, const int32_t* tokens, int64_t n, float* out, q8lin_stream_t stream) {
+  int st = validate_weight(w);
+  if (st != Q8LIN_OK) return st;
+  if (n < 0 || n > (1 << 20)) return fail(Q8LIN_ERR_SHAPE, "token count must be in [0, 2^20]");
+  if (n == 0) return Q8LIN_OK;
+  if (!tokens || !out) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "tokens and out must be non-null device pointers");
+  DeviceGuard guard(w->device);
+  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_embed_rows(*w, tokens, (int)n, out, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "embed launch");
+  return Q8LIN_OK;
+}
+
+int q8lin_rmsnorm(const float* x, const float* weight, int64_t m, int64_t n, float eps, float* y,
+                  q8lin_stream_t stream) {
+  if (m < 0 || n <= 0 || m > (1 << 24)) return fail(Q8LIN_ERR_SHAPE, "rmsnorm needs 0 <= m and n > 0");
+  if (m == 0) return Q8LIN_OK;
+  if (!x || !weight || !y) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "x, weight and y must be non-null device pointers");
+  cudaError_t e = launch_rmsnorm(x, weight, eps, m, n, y, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+  return Q8LIN_OK;
+}
+
+int q8lin_rope_kv(const float* qkv, const int32_t* pos, const float* cos_t, const float* sin_t, float* k_cache,
+                  float* v_cache, int32_t hq, int32_t hkv, int32_t d, int32_t max_t, float* q_out,
+                  q8lin_stream_t stream) {
+  if (hq <= 0 || hkv <= 0 || hq % hkv || d <= 0 || d % 2 || d > 1024 || max_t <= 0)
+    return fail(Q8LIN_ERR_SHAPE, "rope needs hq a positive multiple of hkv, an even d <= 1024 and max_t > 0");
+  if (!qkv || !pos || !cos_t || !sin_t || !k_cache || !v_cache || !q_out)
+    return fail(Q8LIN_ERR_INVALID_ARGUMENT, "rope pointers must be non-null device pointers");
+  cudaError_t e = launch_rope_kv(qkv, pos, cos_t, sin_t, k_cache, v_cache, hq, hkv, d, max_t, q_out,
+                                 reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope launch");
+  return Q8LIN_OK;
+}
+
+size_t q8lin_attention_workspace_size(int32_t hq, int32_t max_t) {
+  if (hq <= 0 || max_t <= 0) return 0;
+  return attention_workspace_bytes(hq, max_t);
+}
+
+int q8lin_attention_decode(const float* q, const float* k_cache, const float* v_cache, const int32_t* pos,
+                           int32_t hq, int32_t hkv, int32_t d, int32_t max_t, void* workspace, size_t workspace_bytes,
+                           float* out, q8lin_stream_t stream) {
+  if (d != 128) return fail(Q8LIN_ERR_SHAPE, "attention_decode supports head width 128");
+  if (hq <= 0 || hkv <= 0 || hq % hkv || max_t <= 0)
+    return fail(Q8LIN_ERR_SHAPE, "attention needs hq a positive multiple of hkv and max_t > 0");
+  if (!q || !k_cache || !v_cache || !pos || !workspace || !out)
+    return fail(Q8LIN_ERR_INVALID_ARGUMENT, "attention pointers must be non-null device pointers");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(Q8LIN_ERR_ALIGNMENT, "q and the caches must be 16-byte aligned");
+  if (workspace_bytes < attention_workspace_bytes(hq, max_t))
+    return fail(Q8LIN_ERR_WORKSPACE, "attention workspace too small (see q8lin_attention_workspace_size)");
+  cudaError_t e = launch_attention_decode(q, k_cache, v_cache, pos, hq, hkv, max_t, workspace, out,
+                                          reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  return Q8LIN_OK;
+}
+
+int q8lin_add(float* x, const float* y, int64_t n, q8lin_stream_t stream) {
+  if (n < 0) return fail(Q8LIN_ERR_SHAPE, "n must be non-negative");
+  if (n == 0) return Q8LIN_OK;
+  if (!x || !y) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "x and y must be non-null device pointers");
+  cudaError_t e = launch_add(x, y, n, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "add launch");
+  return Q8LIN_OK;
+}
+
+size_t q8lin_argmax_workspace_size(void) { return argmax_workspace_bytes(); }
+
+int q8lin_argmax(const float* logits, int64_t n, void* workspace, size_t workspace_bytes, int32_t* token, int32_t* pos,
+                 q8lin_stream_t stream) {
+  if (n <= 0 || n > INT32_MAX) return fail(Q8LIN_ERR_SHAPE, "argmax needs 0 < n < 2^31");
+  if (!logits || !workspace || !token) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "logits, workspace and token must be non-null");
+  if (workspace_bytes < argmax_workspace_bytes())
+    return fail(Q8LIN_ERR_WORKSPACE, "argmax workspace too small (see q8lin_argmax_workspace_size)");
+  cudaError_t e = launch_argmax(logits, (int)n, workspace, token, pos, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
   return Q8LIN_OK;
 }
 

@@ -63,6 +63,19 @@ cudaError_t read_gemv_fault(unsigned int* flags, bool clear);
 // SwiGLU between the MLP projections (mlp.cu): h[m][i] = silu(gu[m][i]) * gu[m][inter + i].
 cudaError_t launch_swiglu(const float* gu, int64_t m, int64_t inter, float* h, cudaStream_t s);
 
+// Decode-step kernels (decoder.cu).  Batch 1; pos and tokens are device ints.
+cudaError_t launch_embed_rows(const q8lin_weight& w, const int* tokens, int n, float* out, cudaStream_t s);
+cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int64_t m, int64_t n, float* y,
+                           cudaStream_t s);
+cudaError_t launch_rope_kv(const float* qkv, const int* pos, const float* cos_t, const float* sin_t, float* kc,
+                           float* vc, int hq, int hkv, int d, int max_t, float* q_out, cudaStream_t s);
+size_t attention_workspace_bytes(int hq, int max_t);
+cudaError_t launch_attention_decode(const float* q, const float* kc, const float* vc, const int* pos, int hq,
+                                    int hkv, int max_t, void* ws, float* out, cudaStream_t s);
+cudaError_t launch_add(float* x, const float* y, int64_t n, cudaStream_t s);
+size_t argmax_workspace_bytes();
+cudaError_t launch_argmax(const float* logits, int n, void* ws, int* token, int* pos, cudaStream_t s);
+
 int sm_count(int device);
 
 // Programmatic dependent launch on/off (env Q8LIN_PDL=0 turns it off; read once).

@@ -1,0 +1,191 @@
+"""Batch-1 Q8_0 decoder (the VoxCPM BaseLM-style Llama decoder).
+
+Per layer (crates/voxcpm/src/transformer.rs:107-155): rms_norm -> fused q|k|v Q8_0 linear
+-> RoPE on q and k, k and v appended to the f32 KV cache -> attention over the cache ->
+o linear -> residual add -> rms_norm -> fused gate|up Q8_0 linear -> SwiGLU -> down
+linear -> residual add; then the final rms_norm, the Q8_0 LM head and the greedy
+argmax.  Every operation is a libq8lin kernel; the position and the current token live
+in device memory, so ``step()`` is capture-safe and one captured CUDA graph replays for
+every decode step (``q8lin_argmax`` writes the next token and advances the position).
+
+Weights are GGUF Q8_0 block arrays (bytes / numpy / torch uint8) and f32 norm vectors;
+q|k|v and gate|up are stored as fused weights (rows q, then k, then v; gate, then up).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check
+from .qmatmul import QMatMul, _stream_ptr
+from .tp_mlp import swiglu
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    hidden: int = 2048
+    layers: int = 28
+    heads: int = 16
+    kv_heads: int = 16
+    head_dim: int = 128
+    inter: int = 6144
+    vocab: int = 73448
+    max_t: int = 640
+    eps: float = 1e-5
+    rope_theta: float = 10000.0
+
+    @property
+    def qkv_rows(self) -> int:
+        return (self.heads + 2 * self.kv_heads) * self.head_dim
+
+
+def rope_tables(cfg: DecoderConfig, factors: Optional[np.ndarray] = None) -> tuple[np.ndarray, np.ndarray]:
+    """cos/sin [max_t][head_dim/2] as transformer.rs:48-60 builds them: freq_i =
+    theta^(-2i/d) in f64 rounded to f32, divided by the factors (f32), angle = pos * freq
+    (f32), then f32 cos/sin."""
+    half = cfg.head_dim // 2
+    freq = np.array([cfg.rope_theta ** (-(2 * i) / cfg.head_dim) for i in range(half)], dtype=np.float64)
+    f = freq.astype(np.float32)
+    if factors is not None:
+        f = (f / np.asarray(factors, dtype=np.float32)).astype(np.float32)
+    pos = np.arange(cfg.max_t, dtype=np.float32)[:, None]
+    ang = (pos * f[None, :]).astype(np.float32)
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+class Q8Decoder:
+    """Weights, KV cache and step buffers of one decoder on one GPU."""
+
+    def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | int | str = 0,
+                 rope_factors: Optional[np.ndarray] = None):
+        if cfg.head_dim != 128:
+            raise _lib.Q8LinError(_lib.ERR_SHAPE, "the decode attention kernel takes head_dim 128")
+        self.cfg = cfg
+        dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        if dev.type != "cuda":
+            raise ValueError("the decoder runs on a CUDA device; there is no CPU path")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        H = cfg.hidden
+
+        def mat(blocks, n, k):
+            return QMatMul.from_gguf_blocks(blocks, n, k, device=dev)
+
+        def vec(v):
+            t = torch.as_tensor(np.asarray(v, dtype=np.float32) if not isinstance(v, torch.Tensor) else v)
+            return t.to(dev, dtype=torch.float32).contiguous()
+
+        self.embed = mat(weights["token_embd"], cfg.vocab, H)
+        self.lm_head = mat(weights["output"], cfg.vocab, H)
+        self.out_norm = vec(weights["output_norm"])
+        self.layers = []
+        for li in range(cfg.layers):
+            w = weights["layers"][li]
+            self.layers.append({
+                "attn_norm": vec(w["attn_norm"]),
+                "qkv": mat(w["qkv"], cfg.qkv_rows, H),
+                "o": mat(w["o"], H, cfg.heads * cfg.head_dim),
+                "ffn_norm": vec(w["ffn_norm"]),
+                "gate_up": mat(w["gate_up"], 2 * cfg.inter, H),
+                "down": mat(w["down"], H, cfg.inter),
+            })
+        cos, sin = rope_tables(cfg, rope_factors)
+        self.cos = torch.from_numpy(cos).to(dev)
+        self.sin = torch.from_numpy(sin).to(dev)
+        kv_shape = (cfg.kv_heads, cfg.max_t, cfg.head_dim)
+        self.k_cache = [torch.zeros(kv_shape, device=dev) for _ in range(cfg.layers)]
+        self.v_cache = [torch.zeros(kv_shape, device=dev) for _ in range(cfg.layers)]
+        f = lambda n: torch.zeros(n, device=dev)
+        self.x, self.h = f(H), f(H)
+        self.qkv, self.q = f(cfg.qkv_rows), f(cfg.heads * cfg.head_dim)
+        self.attn, self.o_out, self.d_out = f(cfg.heads * cfg.head_dim), f(H), f(H)
+        self.gu, self.logits = f(2 * cfg.inter), f(cfg.vocab)
+        self.token = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        L = _lib.lib()
+        self.attn_ws = torch.zeros(L.q8lin_attention_workspace_size(cfg.heads, cfg.max_t), dtype=torch.uint8,
+                                   device=dev)
+        self.argmax_ws = torch.zeros(L.q8lin_argmax_workspace_size(), dtype=torch.uint8, device=dev)
+
+    @staticmethod
+    def _p(t: torch.Tensor) -> ctypes.c_void_p:
+        return ctypes.c_void_p(t.data_ptr())
+
+    def reset(self, token: int = 0) -> None:
+        """Empty the cache (position 0) and set the current token."""
+        self.pos.zero_()
+        self.token.fill_(int(token))
+
+    def step(self) -> None:
+        """One decode step for the token at self.token / position self.pos; afterwards
+        self.token holds the greedy next token, self.logits its logits, pos advanced."""
+        cfg, L, P = self.cfg, _lib.lib(), self._p
+        s = ctypes.c_void_p(_stream_ptr(self.device))
+        H = cfg.hidden
+        check(L.q8lin_embed_rows(self.embed.handle, P(self.token), 1, P(self.x), s))
+        for li, w in enumerate(self.layers):
+            check(L.q8lin_rmsnorm(P(self.x), P(w["attn_norm"]), 1, H, cfg.eps, P(self.h), s))
+            w["qkv"].forward(self.h.view(1, H), out=self.qkv.view(1, -1))
+            check(L.q8lin_rope_kv(P(self.qkv), P(self.pos), P(self.cos), P(self.sin), P(self.k_cache[li]),
+                                  P(self.v_cache[li]), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.max_t,
+                                  P(self.q), s))
+            check(L.q8lin_attention_decode(P(self.q), P(self.k_cache[li]), P(self.v_cache[li]), P(self.pos),
+                                           cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.max_t, P(self.attn_ws),
+                                           self.attn_ws.numel(), P(self.attn), s))
+            w["o"].forward(self.attn.view(1, -1), out=self.o_out.view(1, H))
+            check(L.q8lin_add(P(self.x), P(self.o_out), H, s))
+            check(L.q8lin_rmsnorm(P(self.x), P(w["ffn_norm"]), 1, H, cfg.eps, P(self.h), s))
+            w["gate_up"].forward(self.h.view(1, H), out=self.gu.view(1, -1))
+            w["down"].forward(swiglu(self.gu.view(1, -1), cfg.inter), out=self.d_out.view(1, H))
+            check(L.q8lin_add(P(self.x), P(self.d_out), H, s))
+        check(L.q8lin_rmsnorm(P(self.x), P(self.out_norm), 1, H, cfg.eps, P(self.h), s))
+        self.lm_head.forward(self.h.view(1, H), out=self.logits.view(1, -1))
+        check(L.q8lin_argmax(P(self.logits), cfg.vocab, P(self.argmax_ws), self.argmax_ws.numel(), P(self.token),
+                             P(self.pos), s))
+
+    def launches_per_step(self) -> int:
+        return 1 + self.cfg.layers * 11 + 3
+
+    def weight_bytes_per_step(self) -> int:
+        cfg = self.cfg
+        per_layer = (cfg.qkv_rows + cfg.hidden + 2 * cfg.inter) * cfg.hidden + cfg.hidden * cfg.inter
+        return (cfg.layers * per_layer + cfg.vocab * cfg.hidden) * 34 // 32
+
+
+def synthetic_weights(cfg: DecoderConfig, seed: int = 0, device: Optional[torch.device] = None) -> dict:
+    """Random-init Q8_0 weights with BASELINE's distributions (qs uniform in [-127, 127],
+    d = |N(0, 0.02)| / 127 as f16; norm weights 1), numpy on the host or torch uint8 on
+    `device` (for the 2 GB full-size model)."""
+    def blocks(n, k):
+        nb = k // 32
+        if device is None:
+            from . import synth
+            return synth.q8_0_blocks(rng, n, k)
+        b = torch.empty((n, nb, 34), dtype=torch.uint8, device=device)
+        b[:, :, 2:] = torch.randint(-127, 128, (n, nb, 32), generator=gen, device=device,
+                                    dtype=torch.int8).view(torch.uint8)
+        d = (torch.randn((n, nb), generator=gen, device=device).abs() * (0.02 / 127.0)).half()
+        b[:, :, :2] = d.view(torch.uint8).view(n, nb, 2)
+        return b
+
+    rng = np.random.default_rng(seed)
+    gen = None
+    if device is not None:
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+    H = cfg.hidden
+    ones = np.ones(H, dtype=np.float32)
+    return {
+        "token_embd": blocks(cfg.vocab, H),
+        "output": blocks(cfg.vocab, H),
+        "output_norm": ones,
+        "layers": [{"attn_norm": ones, "qkv": blocks(cfg.qkv_rows, H), "o": blocks(H, cfg.heads * cfg.head_dim),
+                    "ffn_norm": ones, "gate_up": blocks(2 * cfg.inter, H), "down": blocks(H, cfg.inter)}
+                   for _ in range(cfg.layers)],
+    }

@@ -1,0 +1,180 @@
+"""Decode-step kernels and the batch-1 Q8_0 decoder against the CPU reference."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from talechime_b200 import QMatMul, _lib, synth
+from talechime_b200.decoder import DecoderConfig, Q8Decoder, rope_tables, synthetic_weights
+
+pytestmark = pytest.mark.gpu
+
+# Logits pass through one re-quantization of the activations per linear: a last-bit
+# difference upstream can move a value across a Q8_0 rounding boundary, so whole-model
+# logits are compared at this relative L2 bound (each kernel is checked tightly below).
+LOGITS_REL_L2 = 2e-3
+
+
+def _s():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def test_embed_rows_is_the_dequantized_row(oracle_lib, cuda_device):
+    rng = np.random.default_rng(1)
+    w = synth.q8_0_blocks(rng, 50, 256)
+    q = QMatMul.from_gguf_blocks(w, 50, 256, device=cuda_device)
+    toks = torch.tensor([3, 49, 0], dtype=torch.int32, device=cuda_device)
+    out = torch.empty((3, 256), device=cuda_device)
+    _lib.check(_lib.lib().q8lin_embed_rows(q.handle, _p(toks), 3, _p(out), _s()))
+    ref = oracle_lib.dequantize(w, 256)[[3, 49, 0]]
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+def test_rmsnorm_matches_candle_formula(cuda_device):
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((3, 2048)).astype(np.float32)
+    w = rng.uniform(0.5, 1.5, 2048).astype(np.float32)
+    y = torch.empty((3, 2048), device=cuda_device)
+    xd, wd = torch.from_numpy(x).to(cuda_device), torch.from_numpy(w).to(cuda_device)  # kept alive for the launch
+    _lib.check(_lib.lib().q8lin_rmsnorm(_p(xd), _p(wd), 3, 2048, 1e-5, _p(y), _s()))
+    torch.cuda.synchronize()
+    x64 = x.astype(np.float64)
+    ref = x64 / np.sqrt((x64 * x64).mean(axis=1, keepdims=True) + 1e-5) * w
+    assert np.max(np.abs(y.cpu().numpy() - ref)) <= 1e-6 * np.max(np.abs(ref))
+
+
+def test_rope_kv_is_the_reference_rotation(cuda_device):
+    cfg = DecoderConfig(hidden=256, layers=1, heads=4, kv_heads=2, inter=512, vocab=10, max_t=16)
+    cos, sin = rope_tables(cfg)
+    rng = np.random.default_rng(3)
+    qkv = rng.standard_normal(cfg.qkv_rows).astype(np.float32)
+    pos = 7
+    dev = cuda_device
+    kc = torch.zeros((2, 16, 128), device=dev)
+    vc = torch.zeros((2, 16, 128), device=dev)
+    qo = torch.zeros(4 * 128, device=dev)
+    qkv_d, pos_d = torch.from_numpy(qkv).to(dev), torch.tensor([pos], dtype=torch.int32, device=dev)
+    cos_d, sin_d = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    _lib.check(_lib.lib().q8lin_rope_kv(_p(qkv_d), _p(pos_d), _p(cos_d), _p(sin_d), _p(kc), _p(vc),
+                                        4, 2, 128, 16, _p(qo), _s()))
+    torch.cuda.synchronize()
+    c = np.concatenate([cos[pos], cos[pos]])
+    s = np.concatenate([-sin[pos], sin[pos]])
+
+    def rot(x):
+        sw = np.concatenate([x[..., 64:], x[..., :64]], axis=-1)
+        return (x * c).astype(np.float32) + (sw * s).astype(np.float32)
+
+    assert np.array_equal(qo.cpu().numpy(), rot(qkv[:512].reshape(4, 128)).reshape(-1))
+    assert np.array_equal(kc.cpu().numpy()[:, pos], rot(qkv[512:768].reshape(2, 128)))
+    assert np.array_equal(vc.cpu().numpy()[:, pos], qkv[768:].reshape(2, 128))
+    assert not kc.cpu().numpy()[:, :pos].any()
+
+
+@pytest.mark.parametrize("hq,hkv,pos", [(4, 2, 0), (4, 2, 70), (16, 16, 200), (16, 2, 511)])
+def test_attention_decode_matches_softmax(cuda_device, hq, hkv, pos):
+    max_t = 512 if pos < 512 else 640
+    rng = np.random.default_rng(4 + pos)
+    q = rng.standard_normal((hq, 128)).astype(np.float32)
+    k = rng.standard_normal((hkv, max_t, 128)).astype(np.float32)
+    v = rng.standard_normal((hkv, max_t, 128)).astype(np.float32)
+    L, dev = _lib.lib(), cuda_device
+    ws = torch.zeros(L.q8lin_attention_workspace_size(hq, max_t), dtype=torch.uint8, device=dev)
+    out = torch.empty((hq, 128), device=dev)
+    qd, kd, vd = torch.from_numpy(q).to(dev), torch.from_numpy(k).to(dev), torch.from_numpy(v).to(dev)
+    pd = torch.tensor([pos], dtype=torch.int32, device=dev)
+    for _ in range(2):  # the arrival counters must be back at zero after a call
+        _lib.check(L.q8lin_attention_decode(_p(qd), _p(kd), _p(vd), _p(pd), hq, hkv, 128, max_t, _p(ws), ws.numel(),
+                                            _p(out), _s()))
+        got = out.cpu().numpy()
+        ref = np.empty((hq, 128))
+        for h in range(hq):
+            kh = h // (hq // hkv)
+            sc = k[kh, :pos + 1].astype(np.float64) @ q[h] / np.sqrt(128.0)
+            p = np.exp(sc - sc.max())
+            ref[h] = (p / p.sum()) @ v[kh, :pos + 1]
+        assert np.max(np.abs(got - ref)) <= 2e-5 * np.max(np.abs(ref))
+
+
+def test_argmax_picks_lowest_index_of_the_max_and_advances_pos(cuda_device):
+    L, dev = _lib.lib(), cuda_device
+    logits = torch.randn(73448, device=dev)
+    logits[5000] = 10.0
+    logits[60000] = 10.0
+    ws = torch.zeros(L.q8lin_argmax_workspace_size(), dtype=torch.uint8, device=dev)
+    tok = torch.zeros(1, dtype=torch.int32, device=dev)
+    pos = torch.tensor([41], dtype=torch.int32, device=dev)
+    for _ in range(2):
+        _lib.check(L.q8lin_argmax(_p(logits), 73448, _p(ws), ws.numel(), _p(tok), _p(pos), _s()))
+    assert int(tok.item()) == 5000 and int(pos.item()) == 43
+
+
+def _tiny(heads, kv_heads, seed):
+    cfg = DecoderConfig(hidden=256, layers=2, heads=heads, kv_heads=kv_heads, inter=512, vocab=1000, max_t=24)
+    w = synthetic_weights(cfg, seed=seed)
+    rng = np.random.default_rng(seed + 1)
+    w["output_norm"] = rng.uniform(0.5, 1.5, cfg.hidden).astype(np.float32)
+    for lw in w["layers"]:
+        lw["attn_norm"] = rng.uniform(0.5, 1.5, cfg.hidden).astype(np.float32)
+        lw["ffn_norm"] = rng.uniform(0.5, 1.5, cfg.hidden).astype(np.float32)
+    return cfg, w
+
+
+def _rel(a, b):
+    return float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b))
+
+
+@pytest.mark.parametrize("heads,kv_heads", [(2, 2), (4, 2)])
+def test_decoder_steps_match_reference(oracle_lib, cuda_device, heads, kv_heads):
+    from oracle.decoder_ref import DecoderRef
+
+    cfg, w = _tiny(heads, kv_heads, 10 + heads)
+    dec = Q8Decoder(cfg, w, device=cuda_device)
+    cos, sin = rope_tables(cfg)
+    ref = DecoderRef(cfg, w, cos, sin)
+    prefix = [17, 401, 9]
+    dec.reset(prefix[0])
+    tok = prefix[0]
+    for pos in range(12):
+        if pos < len(prefix):
+            tok = prefix[pos]
+            dec.token.fill_(tok)
+        dec.step()
+        lr = ref.step(tok, pos)
+        lg = dec.logits.cpu().numpy()
+        assert _rel(lg, lr) <= LOGITS_REL_L2, f"step {pos}"
+        nxt = int(dec.token.item())
+        assert nxt == int(np.argmax(lr)), f"step {pos}"
+        assert int(dec.pos.item()) == pos + 1
+        tok = nxt
+
+
+def test_decoder_graph_replay_matches_eager(cuda_device):
+    cfg, w = _tiny(4, 2, 30)
+    dec = Q8Decoder(cfg, w, device=cuda_device)
+    stream = torch.cuda.Stream(cuda_device)
+    with torch.cuda.stream(stream):
+        dec.reset(5)
+        eager = []
+        for _ in range(6):
+            dec.step()
+            eager.append(int(dec.token.item()))
+        dec.reset(5)
+        dec.step()  # warm-up outside capture
+        dec.reset(5)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            dec.step()
+        dec.reset(5)
+        replay = []
+        for _ in range(6):
+            g.replay()
+            stream.synchronize()
+            replay.append(int(dec.token.item()))
+    assert replay == eager
