@@ -122,8 +122,8 @@ int q8lin_forward_noalloc(const q8lin_weight* w, const float* x, float* y, int64
 
 /*
  * Device-side fault word of `device` (bit 0: a tensor-core kernel's bounded wait ran
- * out, bit 1: the M = 1 streaming GEMV's, bit 2: the small-batch int8 kernel's; the
- * kernel returned early and its output is invalid).  Reads it with a
+ * out, bit 1: the M = 1 streaming GEMV's, bit 2: the small-batch int8 kernel's, bit 3:
+ * the fused attention's; the kernel returned early and its output is invalid).  Reads it with a
  * device synchronisation; `clear` resets it.  No counterpart in the reference (candle's
  * kernels have no bounded waits); this is the library's failure-detection hook.
  */
@@ -157,6 +157,14 @@ int q8lin_swiglu(const float* gu, int64_t m, int64_t inter, float* h, q8lin_stre
  * attention.rs:28-98 (rms_norm, rotate, KV-cache cat, grouped attention, residual add)
  * and the greedy pick of the decode loop.
  */
+/* The decode-step fusions around one projection (M = 1, K <= 8192), in one kernel:
+ *   prologue 0: y = W . x;  1: y = W . rms_norm(x, norm_weight, eps)  (x[K]);
+ *   2: y = W . (silu(x[0..K)) * x[K..2K))  (gate|up of the fused MLP projection);
+ *   then, if residual != NULL, y = residual + y (residual may alias y).
+ * Replaces norm -> linear and linear -> residual add pairs of
+ * crates/voxcpm/src/transformer.rs:117-118,146-150 with one launch each. */
+int q8lin_forward_fused(const q8lin_weight* w, const float* x, float* y, int64_t m, int32_t prologue,
+                        const float* norm_weight, float eps, const float* residual, q8lin_stream_t stream);
 /* Dequantized rows tokens[0..n) of a Q8_0 embedding weight [vocab][hidden] -> out[n][hidden]. */
 int q8lin_embed_rows(const q8lin_weight* w, const int32_t* tokens, int64_t n, float* out, q8lin_stream_t stream);
 /* y[m][n] = x / sqrt(sum(x^2)/n + eps) * weight (candle_nn::ops::rms_norm). */
@@ -173,6 +181,13 @@ size_t q8lin_attention_workspace_size(int32_t hq, int32_t max_t);
 int q8lin_attention_decode(const float* q, const float* k_cache, const float* v_cache, const int32_t* pos,
                            int32_t hq, int32_t hkv, int32_t d, int32_t max_t, void* workspace, size_t workspace_bytes,
                            float* out, q8lin_stream_t stream);
+size_t q8lin_rope_attention_workspace_size(int32_t hq, int32_t max_t);
+/* RoPE + KV append + attention in one launch: rotates q and the current k of qkv at *pos,
+ * appends k and v to the caches at row *pos and writes out[hq][d] = softmax(q K^T /
+ * sqrt(d)) V over rows [0, *pos]; d = 128.  Workspace zero-filled once before first use. */
+int q8lin_rope_attention_decode(const float* qkv, const int32_t* pos, const float* cos_t, const float* sin_t,
+                                float* k_cache, float* v_cache, int32_t hq, int32_t hkv, int32_t d, int32_t max_t,
+                                void* workspace, size_t workspace_bytes, float* out, q8lin_stream_t stream);
 /* x[0..n) += y[0..n). */
 int q8lin_add(float* x, const float* y, int64_t n, q8lin_stream_t stream);
 size_t q8lin_argmax_workspace_size(void);

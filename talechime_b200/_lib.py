@@ -45,6 +45,8 @@ SIGNATURES = {
     "q8lin_forward_noalloc": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p]),
     "q8lin_fault_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
     "q8lin_swiglu": (ctypes.c_int, [_c_p, _i64, _i64, _c_p, _c_p]),
+    "q8lin_forward_fused": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, ctypes.c_int32, _c_p, ctypes.c_float, _c_p,
+                                           _c_p]),
     "q8lin_embed_rows": (ctypes.c_int, [_c_p, _c_p, _i64, _c_p, _c_p]),
     "q8lin_rmsnorm": (ctypes.c_int, [_c_p, _c_p, _i64, _i64, ctypes.c_float, _c_p, _c_p]),
     "q8lin_rope_kv": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_int32, ctypes.c_int32,
@@ -52,6 +54,9 @@ SIGNATURES = {
     "q8lin_attention_workspace_size": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32]),
     "q8lin_attention_decode": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_int32, ctypes.c_int32, _c_p, ctypes.c_size_t, _c_p, _c_p]),
+    "q8lin_rope_attention_workspace_size": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32]),
+    "q8lin_rope_attention_decode": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_int32, ctypes.c_int32,
+                                                   ctypes.c_int32, ctypes.c_int32, _c_p, ctypes.c_size_t, _c_p, _c_p]),
     "q8lin_add": (ctypes.c_int, [_c_p, _c_p, _i64, _c_p]),
     "q8lin_argmax_workspace_size": (ctypes.c_size_t, []),
     "q8lin_argmax": (ctypes.c_int, [_c_p, _i64, _c_p, ctypes.c_size_t, _c_p, _c_p, _c_p]),

@@ -351,12 +351,13 @@ int q8lin_fault_status(int device, uint32_t* flags, int clear) {
   int st = check_device(device);
   if (st != Q8LIN_OK) return st;
   DeviceGuard guard(device);
-  unsigned int f = 0, g = 0, h = 0;
+  unsigned int f = 0, g = 0, h = 0, a = 0;
   cudaError_t e = read_tc_fault(&f, clear != 0);
   if (e == cudaSuccess) e = read_gemv_fault(&g, clear != 0);
   if (e == cudaSuccess) e = read_skinny_fault(&h, clear != 0);
+  if (e == cudaSuccess) e = read_attention_fault(&a, clear != 0);
   if (e != cudaSuccess) return cuda_fail(e, "read fault word");
-  *flags = f | g | h;
+  *flags = f | g | h | a;
   return Q8LIN_OK;
 }
 
@@ -380,6 +381,31 @@ int q8lin_swiglu(const float* gu, int64_t m, int64_t inter, float* h, q8lin_stre
     return fail(Q8LIN_ERR_ALIGNMENT, "gu and h must be 4-byte aligned");
   cudaError_t e = launch_swiglu(gu, m, inter, h, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "swiglu launch");
+  return Q8LIN_OK;
+}
+
+int q8lin_forward_fused(const q8lin_weight* w, const float* x, float* y, int64_t m, int32_t prologue,
+                        const float* norm_weight, float eps, const float* residual, q8lin_stream_t stream) {
+  int st = validate_weight(w);
+  if (st != Q8LIN_OK) return st;
+  if (m != 1) return fail(Q8LIN_ERR_SHAPE, "the fused forms take one activation row (decode), got M=" + std::to_string(m));
+  if (w->k > kFusedMaxK) return fail(Q8LIN_ERR_SHAPE, "the fused forms need K <= 8192");
+  if (prologue < kPrologueNone || prologue > kPrologueSwiGLU) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "unknown prologue");
+  if (!x || !y) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "x and y must be non-null device pointers");
+  if (!aligned16(x) || !aligned16(y)) return fail(Q8LIN_ERR_ALIGNMENT, "x and y must be 16-byte aligned");
+  if (prologue == kPrologueRmsNorm && (!norm_weight || !aligned16(norm_weight)))
+    return fail(Q8LIN_ERR_INVALID_ARGUMENT, "the rms_norm prologue needs a 16-byte aligned norm weight");
+  if (residual && (reinterpret_cast<uintptr_t>(residual) & 3u))
+    return fail(Q8LIN_ERR_ALIGNMENT, "residual must be 4-byte aligned");
+  DeviceGuard guard(w->device);
+  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
+  GemvFusion f;
+  f.prologue = prologue;
+  f.norm_w = norm_weight;
+  f.eps = eps;
+  f.residual = residual;
+  cudaError_t e = launch_gemv_fused(*w, x, y, f, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fused gemv launch");
   return Q8LIN_OK;
 }
 
@@ -439,6 +465,30 @@ int q8lin_attention_decode(const float* q, const float* k_cache, const float* v_
   cudaError_t e = launch_attention_decode(q, k_cache, v_cache, pos, hq, hkv, max_t, workspace, out,
                                           reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  return Q8LIN_OK;
+}
+
+size_t q8lin_rope_attention_workspace_size(int32_t hq, int32_t max_t) {
+  if (hq <= 0 || max_t <= 0) return 0;
+  return rope_attention_workspace_bytes(hq, max_t);
+}
+
+int q8lin_rope_attention_decode(const float* qkv, const int32_t* pos, const float* cos_t, const float* sin_t,
+                                float* k_cache, float* v_cache, int32_t hq, int32_t hkv, int32_t d, int32_t max_t,
+                                void* workspace, size_t workspace_bytes, float* out, q8lin_stream_t stream) {
+  if (d != 128) return fail(Q8LIN_ERR_SHAPE, "rope_attention_decode supports head width 128");
+  if (hq <= 0 || hkv <= 0 || hq % hkv || max_t <= 0)
+    return fail(Q8LIN_ERR_SHAPE, "attention needs hq a positive multiple of hkv and max_t > 0");
+  if (!qkv || !pos || !cos_t || !sin_t || !k_cache || !v_cache || !workspace || !out)
+    return fail(Q8LIN_ERR_INVALID_ARGUMENT, "rope_attention pointers must be non-null device pointers");
+  if (!aligned16(k_cache) || !aligned16(v_cache)) return fail(Q8LIN_ERR_ALIGNMENT, "the caches must be 16-byte aligned");
+  if (workspace_bytes < rope_attention_workspace_bytes(hq, max_t))
+    return fail(Q8LIN_ERR_WORKSPACE, "attention workspace too small (see q8lin_rope_attention_workspace_size)");
+  int device = 0;
+  cudaGetDevice(&device);
+  cudaError_t e = launch_rope_attention(qkv, pos, cos_t, sin_t, k_cache, v_cache, hq, hkv, max_t, workspace, out,
+                                        device, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope_attention launch");
   return Q8LIN_OK;
 }
 

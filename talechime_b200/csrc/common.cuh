@@ -124,6 +124,12 @@ __device__ __forceinline__ int quantize_octet(const float4 v, __half& d_h) {
   return (a & 0xff) | ((b & 0xff) << 8) | ((c & 0xff) << 16) | ((d & 0xff) << 24);
 }
 
+// candle's f32 silu(g) = g / (1 + exp(-g)), times u; each operation rounded (exp is
+// CUDA's expf, within 2 ulp of exp).
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);

@@ -115,7 +115,7 @@ attention_decode_kernel(const float* __restrict__ q, const float* __restrict__ k
   pdl_wait();
   const int h = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
   const int hk = h / (Hq / Hkv);
-  const int len = *pos_dev + 1;
+  const int len = min(*pos_dev + 1, max_t);  // never past the cache
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float4 q4 = reinterpret_cast<const float4*>(q + (size_t)h * D)[lane];
   const float* kh = kc + (size_t)hk * max_t * D;
@@ -184,6 +184,189 @@ attention_decode_kernel(const float* __restrict__ q, const float* __restrict__ k
       out[(size_t)h * D + threadIdx.x] = __fdiv_rn(A, L);
     }
     if (threadIdx.x == 0) cnt[h] = 0;
+  }
+  pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------------------------
+// RoPE + KV append + attention in one kernel (the decode step's attention block).
+// grid (Hq, splits of kRaPositions positions); 256 threads.  A CTA:
+//   * bulk-copies the cached K and V rows [t0, min(t1, pos)) of its kv head into shared
+//     memory (one cp.async.bulk each, mbarrier complete_tx);
+//   * meanwhile rotates q of its head and, if its range holds the current position, k and
+//     v of the current token straight from the qkv projection (so no CTA reads a cache
+//     row another CTA of this launch writes); the first q head of each kv head appends
+//     k and v to the cache;
+//   * scores 4 positions per warp at a time, softmax within the CTA (max, exp, sum), the
+//     weighted sum of V by 256 threads (two position halves per dimension), and writes
+//     its (max, sum, acc[128]) partial; the last CTA of the head merges the partials in
+//     split order and writes the output.
+constexpr int kRaPositions = 64;
+constexpr int kRaThreads = 256;
+constexpr uint32_t kRaSpin = 1u << 24;
+
+__device__ unsigned int g_attn_fault;
+
+struct RaSmem {
+  alignas(16) float k[kRaPositions][128];
+  alignas(16) float v[kRaPositions][128];
+  alignas(16) float q[128];
+  alignas(16) float kcur[128];
+  alignas(16) float vcur[128];
+  alignas(16) float acc2[2][128];
+  float sc[kRaPositions];
+  float red[8];
+  alignas(8) uint64_t bar;
+  int last;
+};
+
+__global__ void __launch_bounds__(kRaThreads)
+rope_attention_kernel(const float* __restrict__ qkv, const int* __restrict__ pos_dev, const float* __restrict__ cos_t,
+                      const float* __restrict__ sin_t, float* __restrict__ kc, float* __restrict__ vc, int Hq, int Hkv,
+                      int max_t, float scale, float* __restrict__ part, unsigned int* __restrict__ cnt,
+                      float* __restrict__ out) {
+  constexpr int D = 128, half = 64;
+  extern __shared__ __align__(16) uint8_t ra_raw[];
+  RaSmem& sm = *reinterpret_cast<RaSmem*>(ra_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
+  const int group = Hq / Hkv, hk = h / group;
+  pdl_wait();
+  const int pos = *pos_dev;
+  const int t0 = split * kRaPositions;
+  const int t1 = min(min(pos + 1, max_t), t0 + kRaPositions);  // never past the cache
+  const int nhere = t1 > t0 ? t1 - t0 : 0;
+  const int rows = min(t1, pos) - t0 > 0 ? min(t1, pos) - t0 : 0;  // cached rows in range
+  const bool cur = t0 <= pos && pos < t1;
+  const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&sm.bar);
+  if (tid == 0 && rows > 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(1) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    const uint32_t bytes = (uint32_t)rows * D * 4;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
+    const float* ks = kc + ((size_t)hk * max_t + t0) * D;
+    const float* vs = vc + ((size_t)hk * max_t + t0) * D;
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"((uint32_t)__cvta_generic_to_shared(&sm.k[0][0])), "l"(ks), "r"(bytes), "r"(bar) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"((uint32_t)__cvta_generic_to_shared(&sm.v[0][0])), "l"(vs), "r"(bytes), "r"(bar) : "memory");
+  }
+  // rotation x*[cos,cos] + [second,first]*[-sin,sin] at the current position
+  if (tid < D && pos >= 0 && pos < max_t) {
+    const int j = tid < half ? tid : tid - half;
+    const float c = cos_t[(size_t)pos * half + j], sn = sin_t[(size_t)pos * half + j];
+    auto rot = [&](const float* xh) {
+      return tid < half ? __fadd_rn(__fmul_rn(xh[tid], c), __fmul_rn(xh[tid + half], -sn))
+                        : __fadd_rn(__fmul_rn(xh[tid], c), __fmul_rn(xh[tid - half], sn));
+    };
+    sm.q[tid] = rot(qkv + (size_t)h * D);
+    if (cur) {
+      const float kr = rot(qkv + (size_t)(Hq + hk) * D);
+      const float vr = qkv[(size_t)(Hq + Hkv + hk) * D + tid];
+      sm.kcur[tid] = kr;
+      sm.vcur[tid] = vr;
+      if (h % group == 0) {  // one writer per kv head
+        kc[((size_t)hk * max_t + pos) * D + tid] = kr;
+        vc[((size_t)hk * max_t + pos) * D + tid] = vr;
+      }
+    }
+  }
+  __syncthreads();
+  bool ok = true;
+  if (rows > 0) {
+    ok = false;
+    for (uint32_t i = 0; i < kRaSpin && !ok; ++i) {
+      uint32_t done;
+      asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n selp.u32 %0, 1, 0, p;\n}"
+                   : "=r"(done) : "r"(bar) : "memory");
+      ok = done != 0;
+    }
+    if (!ok && tid == 0) atomicOr(&g_attn_fault, 8u);
+  }
+  // scores: warp w takes positions w*8 .. w*8+7, four at a time
+  const float4 q4 = reinterpret_cast<const float4*>(sm.q)[lane];
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    float s[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = warp * 8 + g * 4 + u;
+      const float* krow = (t0 + j == pos) ? sm.kcur : sm.k[j < rows ? j : 0];
+      const float4 k4 = reinterpret_cast<const float4*>(krow)[lane];
+      float d = __fmul_rn(q4.x, k4.x);
+      d = __fadd_rn(d, __fmul_rn(q4.y, k4.y));
+      d = __fadd_rn(d, __fmul_rn(q4.z, k4.z));
+      s[u] = __fadd_rn(d, __fmul_rn(q4.w, k4.w));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) s[u] += __shfl_xor_sync(kFull, s[u], o);
+    if (lane == 0)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = warp * 8 + g * 4 + u;
+        sm.sc[j] = (j < nhere && ok) ? __fmul_rn(s[u], scale) : -INFINITY;
+      }
+  }
+  __syncthreads();
+  // softmax within the CTA: warp 0 reduces max and sum over the 64 scores
+  if (warp == 0) {
+    const float a = sm.sc[lane], b = sm.sc[lane + 32];
+    float mx = fmaxf(a, b);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+    const float pa = (a == -INFINITY) ? 0.0f : expf(a - mx);
+    const float pb = (b == -INFINITY) ? 0.0f : expf(b - mx);
+    sm.sc[lane] = pa;
+    sm.sc[lane + 32] = pb;
+    const float l = warp_sum(__fadd_rn(pa, pb));
+    if (lane == 0) {
+      sm.red[0] = mx;
+      sm.red[1] = l;
+    }
+  }
+  __syncthreads();
+  // weighted sum of V: dimension tid % 128, positions half (tid / 128) * 32 .. +32
+  {
+    const int d = tid & 127, hh = tid >> 7;
+    float a = 0.0f;
+    for (int j = hh * 32; j < hh * 32 + 32; ++j) {
+      const float p = sm.sc[j];
+      if (p != 0.0f) {
+        const float vv = (t0 + j == pos) ? sm.vcur[d] : sm.v[j < rows ? j : 0][d];
+        a = __fadd_rn(a, __fmul_rn(p, vv));
+      }
+    }
+    sm.acc2[hh][d] = a;
+  }
+  __syncthreads();
+  float* mine = part + ((size_t)h * splits + split) * (2 + D);
+  if (tid < D) mine[2 + tid] = __fadd_rn(sm.acc2[0][tid], sm.acc2[1][tid]);
+  if (tid == 0) {
+    mine[0] = nhere > 0 ? sm.red[0] : -INFINITY;
+    mine[1] = nhere > 0 ? sm.red[1] : 0.0f;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) sm.last = (atomicAdd(&cnt[h], 1u) == (unsigned)(splits - 1)) ? 1 : 0;
+  __syncthreads();
+  if (sm.last) {
+    __threadfence();
+    const float* base = part + (size_t)h * splits * (2 + D);
+    if (tid < D) {
+      float M = -INFINITY;
+      for (int s = 0; s < splits; ++s) M = fmaxf(M, base[(size_t)s * (2 + D)]);
+      float L = 0.0f, A = 0.0f;
+      for (int s = 0; s < splits; ++s) {
+        const float ms = base[(size_t)s * (2 + D)];
+        const float f = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+        L = __fadd_rn(L, __fmul_rn(base[(size_t)s * (2 + D) + 1], f));
+        A = __fadd_rn(A, __fmul_rn(base[(size_t)s * (2 + D) + 2 + tid], f));
+      }
+      out[(size_t)h * D + tid] = __fdiv_rn(A, L);
+    }
+    if (tid == 0) cnt[h] = 0;
   }
   pdl_launch_dependents();
 }
@@ -290,6 +473,43 @@ cudaError_t launch_attention_decode(const float* q, const float* kc, const float
   // candle's `scores / sqrt(width)` multiplies by the f32 rounding of 1/sqrt(width)
   const float scale = (float)(1.0 / std::sqrt(128.0));
   return cudaLaunchKernelEx(&cfg, attention_decode_kernel, q, kc, vc, pos, hq, hkv, max_t, scale, part, cnt, out);
+}
+
+size_t rope_attention_workspace_bytes(int hq, int max_t) {
+  const int splits = (max_t + kRaPositions - 1) / kRaPositions;
+  return ((size_t)hq * splits * (2 + 128) * 4 + 255) / 256 * 256 + ((size_t)hq * 4 + 255) / 256 * 256;
+}
+
+cudaError_t launch_rope_attention(const float* qkv, const int* pos, const float* cos_t, const float* sin_t, float* kc,
+                                  float* vc, int hq, int hkv, int max_t, void* ws, float* out, int device,
+                                  cudaStream_t s) {
+  const int splits = (max_t + kRaPositions - 1) / kRaPositions;
+  float* part = static_cast<float*>(ws);
+  unsigned int* cnt = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(ws) +
+                                                      ((size_t)hq * splits * (2 + 128) * 4 + 255) / 256 * 256);
+  static int configured[128] = {0};
+  const int dev = (device >= 0 && device < 128) ? device : 0;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(rope_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(RaSmem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = 1;
+  }
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_cfg(dim3((unsigned)hq, (unsigned)splits), dim3(kRaThreads), s, attr);
+  cfg.dynamicSmemBytes = sizeof(RaSmem);
+  const float scale = (float)(1.0 / std::sqrt(128.0));
+  return cudaLaunchKernelEx(&cfg, rope_attention_kernel, qkv, pos, cos_t, sin_t, kc, vc, hq, hkv, max_t, scale, part,
+                            cnt, out);
+}
+
+cudaError_t read_attention_fault(unsigned int* flags, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(flags, g_attn_fault, sizeof(unsigned int));
+  if (e == cudaSuccess && clear) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_attn_fault, &z, sizeof(z));
+  }
+  return e;
 }
 
 cudaError_t launch_add(float* x, const float* y, int64_t n, cudaStream_t s) {

@@ -215,7 +215,7 @@ __device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
 
 __global__ void __launch_bounds__(kStreamThreads, 2)
 gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, const float* __restrict__ x,
-                        float* __restrict__ y, int rpc, int slots) {
+                        float* __restrict__ y, int rpc, int slots, const GemvFusion fz) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int nb = K >> 5;
   const int nunits = K >> 4;  // 16-byte units per row; unit u is half of block u / 2
@@ -280,11 +280,56 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
     constexpr int kT = kConsumerWarps * 32;
     constexpr int kQG = 4;
     const int nquads = nb * 8;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
     float4 v[kQG];
+    if (fz.prologue == kPrologueSwiGLU) {
+      // x = [gate | up], K values each: the activation is silu(gate) * up
 #pragma unroll
-    for (int g = 0; g < kQG; ++g) {
-      const int i = g * kT + threadIdx.x;
-      v[g] = i < nquads ? __ldg(reinterpret_cast<const float4*>(x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int g = 0; g < kQG; ++g) {
+        const int i = g * kT + threadIdx.x;
+        if (i < nquads) {
+          const float4 ga = __ldg(x4 + i), ua = __ldg(x4 + nquads + i);
+          v[g] = make_float4(silu_mul(ga.x, ua.x), silu_mul(ga.y, ua.y), silu_mul(ga.z, ua.z), silu_mul(ga.w, ua.w));
+        } else {
+          v[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < kQG; ++g) {
+        const int i = g * kT + threadIdx.x;
+        v[g] = i < nquads ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    if (fz.prologue == kPrologueRmsNorm) {
+      // rms_norm over the row: sum of squares across the consumer warps (tree order),
+      // m = sqrt(sum/K + eps), x -> (x / m) * w
+      __shared__ float red[kConsumerWarps];
+      float sq = 0.0f;
+#pragma unroll
+      for (int g = 0; g < kQG; ++g) {
+        sq = __fadd_rn(sq, __fmul_rn(v[g].x, v[g].x));
+        sq = __fadd_rn(sq, __fmul_rn(v[g].y, v[g].y));
+        sq = __fadd_rn(sq, __fmul_rn(v[g].z, v[g].z));
+        sq = __fadd_rn(sq, __fmul_rn(v[g].w, v[g].w));
+      }
+      sq = warp_sum(sq);
+      if (lane == 0) red[warp] = sq;
+      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      float total = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kConsumerWarps; ++i) total += red[i];
+      const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)K), fz.eps));
+      const float4* w4 = reinterpret_cast<const float4*>(fz.norm_w);
+#pragma unroll
+      for (int g = 0; g < kQG; ++g) {
+        const int i = g * kT + threadIdx.x;
+        if (i < nquads) {
+          const float4 wv = __ldg(w4 + i);
+          v[g] = make_float4(__fmul_rn(__fdiv_rn(v[g].x, m), wv.x), __fmul_rn(__fdiv_rn(v[g].y, m), wv.y),
+                             __fmul_rn(__fdiv_rn(v[g].z, m), wv.z), __fmul_rn(__fdiv_rn(v[g].w, m), wv.w));
+        }
+      }
     }
 #pragma unroll
     for (int g = 0; g < kQG; ++g) {
@@ -341,7 +386,7 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
     __syncwarp();
     if (lane == 0) {
       if (nseg == 1) {
-        y[r0 + rr] = accs;
+        y[r0 + rr] = fz.residual ? __fadd_rn(fz.residual[r0 + rr], accs) : accs;
       } else {
         float* pr = part + (slot * kMaxRpc + ri) * kMaxSegs;
         pr[seg] = accs;
@@ -350,7 +395,7 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
           __threadfence_block();
           float sum = pr[0];
           for (int q = 1; q < nseg; ++q) sum += pr[q];
-          y[r0 + rr] = sum;
+          y[r0 + rr] = fz.residual ? __fadd_rn(fz.residual[r0 + rr], sum) : sum;
           cnt[slot * kMaxRpc + ri] = 0;
         }
       }
@@ -375,7 +420,8 @@ size_t stream_smem_bytes(int64_t k) {
                   kMaxSlots * kMaxRpc * 4 + 2 * kMaxSlots * 8);
 }
 
-cudaError_t launch_stream(const q8lin_weight& w, const float* x, float* y, int rpc, int slots, cudaStream_t s) {
+cudaError_t launch_stream(const q8lin_weight& w, const float* x, float* y, int rpc, int slots, cudaStream_t s,
+                          const GemvFusion& fz = GemvFusion()) {
   const int K = (int)w.k, N = (int)w.n;
   const size_t smem = stream_smem_bytes(K);
   static int configured_smem[128] = {0};
@@ -404,7 +450,7 @@ cudaError_t launch_stream(const q8lin_weight& w, const float* x, float* y, int r
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, gemv_q8_0_stream_kernel, (const uint8_t*)w.packed, w.row_stride, N, K, x, y, rpc,
-                            slots);
+                            slots, fz);
 }
 
 template <int M>
@@ -449,6 +495,13 @@ cudaError_t read_gemv_fault(unsigned int* flags, bool clear) {
     e = cudaMemcpyToSymbol(g_gemv_fault, &z, sizeof(z));
   }
   return e;
+}
+
+cudaError_t launch_gemv_fused(const q8lin_weight& w, const float* x, float* y, const GemvFusion& f, cudaStream_t s) {
+  int rpc, slots;
+  stream_plan(w.k, w.row_stride, &rpc, &slots);
+  if (slots == 0 || w.k > kFusedMaxK) return cudaErrorInvalidValue;
+  return launch_stream(w, x, y, rpc, slots, s, f);
 }
 
 cudaError_t launch_gemv(const q8lin_weight& w, const float* x, float* y, int m, cudaStream_t s) {

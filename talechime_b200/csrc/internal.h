@@ -32,6 +32,21 @@ cudaError_t launch_dequantize(const uint8_t* packed, float* out, int64_t n, int6
 cudaError_t launch_quantize_rows(const float* x, int64_t m, int64_t k, int8_t* qs,
                                  uint16_t* d_f16, float* d_f32, cudaStream_t s);
 
+// Optional prologue / epilogue of the M = 1 streaming GEMV (decode step fusions):
+// prologue kRmsNorm: x -> x / sqrt(sum(x^2)/K + eps) * norm_w before quantization;
+// prologue kSwiGLU: x holds gate|up [2K] -> silu(gate) * up; epilogue: y = residual + W.x
+// (residual may alias y).
+enum GemvPrologue : int { kPrologueNone = 0, kPrologueRmsNorm = 1, kPrologueSwiGLU = 2 };
+struct GemvFusion {
+  int prologue = kPrologueNone;
+  const float* norm_w = nullptr;
+  float eps = 0.0f;
+  const float* residual = nullptr;
+};
+// The fused forms need the streaming kernel: M = 1 and K <= this bound.
+constexpr int kFusedMaxK = 8192;
+cudaError_t launch_gemv_fused(const q8lin_weight& w, const float* x, float* y, const GemvFusion& f, cudaStream_t s);
+
 // Decode GEMV for 1 <= m <= kGemvMaxM.
 constexpr int kGemvMaxM = 16;
 size_t gemv_smem_bytes(int m, int64_t k);
@@ -72,6 +87,11 @@ cudaError_t launch_rope_kv(const float* qkv, const int* pos, const float* cos_t,
 size_t attention_workspace_bytes(int hq, int max_t);
 cudaError_t launch_attention_decode(const float* q, const float* kc, const float* vc, const int* pos, int hq,
                                     int hkv, int max_t, void* ws, float* out, cudaStream_t s);
+size_t rope_attention_workspace_bytes(int hq, int max_t);
+cudaError_t launch_rope_attention(const float* qkv, const int* pos, const float* cos_t, const float* sin_t, float* kc,
+                                  float* vc, int hq, int hkv, int max_t, void* ws, float* out, int device,
+                                  cudaStream_t s);
+cudaError_t read_attention_fault(unsigned int* flags, bool clear);  // bit 3
 cudaError_t launch_add(float* x, const float* y, int64_t n, cudaStream_t s);
 size_t argmax_workspace_bytes();
 cudaError_t launch_argmax(const float* logits, int n, void* ws, int* token, int* pos, cudaStream_t s);

@@ -14,11 +14,6 @@ namespace q8lin {
 
 namespace {
 
-__device__ __forceinline__ float silu_mul(float g, float u) {
-  const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-  return __fmul_rn(s, u);
-}
-
 // Four outputs per thread when I is a multiple of 4 (rows then start on 16 bytes).
 __global__ void swiglu4_kernel(const float* __restrict__ gu, int64_t m, int64_t inter, float* __restrict__ h) {
   const int64_t q = inter / 4;

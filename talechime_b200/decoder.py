@@ -4,7 +4,8 @@ Per layer (crates/voxcpm/src/transformer.rs:107-155): rms_norm -> fused q|k|v Q8
 -> RoPE on q and k, k and v appended to the f32 KV cache -> attention over the cache ->
 o linear -> residual add -> rms_norm -> fused gate|up Q8_0 linear -> SwiGLU -> down
 linear -> residual add; then the final rms_norm, the Q8_0 LM head and the greedy
-argmax.  Every operation is a libq8lin kernel; the position and the current token live
+argmax.  Every operation is a libq8lin kernel (by default with the norms, SwiGLU and
+residual adds fused into the projections); the position and the current token live
 in device memory, so ``step()`` is capture-safe and one captured CUDA graph replays for
 every decode step (``q8lin_argmax`` writes the next token and advances the position).
 
@@ -112,6 +113,8 @@ class Q8Decoder:
         self.attn_ws = torch.zeros(L.q8lin_attention_workspace_size(cfg.heads, cfg.max_t), dtype=torch.uint8,
                                    device=dev)
         self.argmax_ws = torch.zeros(L.q8lin_argmax_workspace_size(), dtype=torch.uint8, device=dev)
+        self.ra_ws = torch.zeros(L.q8lin_rope_attention_workspace_size(cfg.heads, cfg.max_t), dtype=torch.uint8,
+                                 device=dev)
 
     @staticmethod
     def _p(t: torch.Tensor) -> ctypes.c_void_p:
@@ -122,9 +125,35 @@ class Q8Decoder:
         self.pos.zero_()
         self.token.fill_(int(token))
 
-    def step(self) -> None:
+    def step(self, fused: bool = True) -> None:
         """One decode step for the token at self.token / position self.pos; afterwards
-        self.token holds the greedy next token, self.logits its logits, pos advanced."""
+        self.token holds the greedy next token, self.logits its logits, pos advanced.
+        fused: rms_norm and SwiGLU run inside the following projection's activation
+        quantization, the residual adds inside the o / down projections and RoPE + KV
+        append inside the attention kernel (5 launches per layer instead of 11)."""
+        if fused:
+            self._step_fused()
+        else:
+            self._step_unfused()
+
+    def _step_fused(self) -> None:
+        cfg, L, P = self.cfg, _lib.lib(), self._p
+        s = ctypes.c_void_p(_stream_ptr(self.device))
+        check(L.q8lin_embed_rows(self.embed.handle, P(self.token), 1, P(self.x), s))
+        for li, w in enumerate(self.layers):
+            w["qkv"].forward_fused(self.x, self.qkv, QMatMul.PROLOGUE_RMSNORM, w["attn_norm"], cfg.eps)
+            check(L.q8lin_rope_attention_decode(P(self.qkv), P(self.pos), P(self.cos), P(self.sin),
+                                                P(self.k_cache[li]), P(self.v_cache[li]), cfg.heads, cfg.kv_heads,
+                                                cfg.head_dim, cfg.max_t, P(self.ra_ws), self.ra_ws.numel(),
+                                                P(self.attn), s))
+            w["o"].forward_fused(self.attn, self.x, residual=self.x)
+            w["gate_up"].forward_fused(self.x, self.gu, QMatMul.PROLOGUE_RMSNORM, w["ffn_norm"], cfg.eps)
+            w["down"].forward_fused(self.gu, self.x, QMatMul.PROLOGUE_SWIGLU, residual=self.x)
+        self.lm_head.forward_fused(self.x, self.logits, QMatMul.PROLOGUE_RMSNORM, self.out_norm, cfg.eps)
+        check(L.q8lin_argmax(P(self.logits), cfg.vocab, P(self.argmax_ws), self.argmax_ws.numel(), P(self.token),
+                             P(self.pos), s))
+
+    def _step_unfused(self) -> None:
         cfg, L, P = self.cfg, _lib.lib(), self._p
         s = ctypes.c_void_p(_stream_ptr(self.device))
         H = cfg.hidden
@@ -149,8 +178,8 @@ class Q8Decoder:
         check(L.q8lin_argmax(P(self.logits), cfg.vocab, P(self.argmax_ws), self.argmax_ws.numel(), P(self.token),
                              P(self.pos), s))
 
-    def launches_per_step(self) -> int:
-        return 1 + self.cfg.layers * 11 + 3
+    def launches_per_step(self, fused: bool = True) -> int:
+        return 1 + self.cfg.layers * (5 if fused else 11) + (2 if fused else 3)
 
     def weight_bytes_per_step(self) -> int:
         cfg = self.cfg

@@ -139,6 +139,26 @@ class QMatMul:
 
     __call__ = forward
 
+    PROLOGUE_NONE, PROLOGUE_RMSNORM, PROLOGUE_SWIGLU = 0, 1, 2
+
+    def forward_fused(self, x: torch.Tensor, out: torch.Tensor, prologue: int = 0,
+                      norm_weight: Optional[torch.Tensor] = None, eps: float = 1e-5,
+                      residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Decode-step fusion (one activation row): out = [residual +] W . p(x) with p the
+        identity, rms_norm(x, norm_weight, eps) or silu(x[:K]) * x[K:]  (q8lin_forward_fused)."""
+        kx = 2 * self.k if prologue == self.PROLOGUE_SWIGLU else self.k
+        for name, t, want in (("x", x, kx), ("out", out, self.n), ("norm_weight", norm_weight, self.k),
+                              ("residual", residual, self.n)):
+            if t is None:
+                continue
+            if t.numel() != want or t.dtype != torch.float32 or not t.is_contiguous() or t.device != self.device:
+                raise Q8LinError(_lib.ERR_SHAPE, f"{name} must be a contiguous f32 tensor of {want} values on "
+                                                 f"{self.device} (one activation row)")
+        ptr = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+        check(_lib.lib().q8lin_forward_fused(self._handle, ptr(x), ptr(out), 1, int(prologue), ptr(norm_weight),
+                                             float(eps), ptr(residual), ctypes.c_void_p(_stream_ptr(self.device))))
+        return out
+
     def dequantize(self) -> torch.Tensor:
         """f32 [N, K] (QTensor::dequantize, crates/voxcpm/src/weights.rs:79-80,106)."""
         out = torch.empty((self.n, self.k), dtype=torch.float32, device=self.device)

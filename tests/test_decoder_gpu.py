@@ -101,6 +101,51 @@ def test_attention_decode_matches_softmax(cuda_device, hq, hkv, pos):
         assert np.max(np.abs(got - ref)) <= 2e-5 * np.max(np.abs(ref))
 
 
+@pytest.mark.parametrize("hq,hkv,max_t,pos", [(4, 2, 24, 0), (4, 2, 24, 23), (16, 16, 640, 63), (16, 16, 640, 64),
+                                              (16, 2, 640, 300), (8, 8, 200, 199)])
+def test_rope_attention_is_rope_then_attention(cuda_device, hq, hkv, max_t, pos):
+    """The fused kernel: rotated q/k, the new k/v row appended, softmax over [0, pos]."""
+    cfg = DecoderConfig(hidden=256, layers=1, heads=hq, kv_heads=hkv, inter=512, vocab=10, max_t=max_t)
+    cos, sin = rope_tables(cfg)
+    rng = np.random.default_rng(100 + pos)
+    qkv = rng.standard_normal(cfg.qkv_rows).astype(np.float32)
+    k = rng.standard_normal((hkv, max_t, 128)).astype(np.float32)
+    v = rng.standard_normal((hkv, max_t, 128)).astype(np.float32)
+    L, dev = _lib.lib(), cuda_device
+    ws = torch.zeros(L.q8lin_rope_attention_workspace_size(hq, max_t), dtype=torch.uint8, device=dev)
+    out = torch.empty((hq, 128), device=dev)
+    qkv_d, pos_d = torch.from_numpy(qkv).to(dev), torch.tensor([pos], dtype=torch.int32, device=dev)
+    cos_d, sin_d = torch.from_numpy(cos).to(dev), torch.from_numpy(sin).to(dev)
+    c = np.concatenate([cos[pos], cos[pos]])
+    s = np.concatenate([-sin[pos], sin[pos]])
+
+    def rot(x):
+        sw = np.concatenate([x[..., 64:], x[..., :64]], axis=-1)
+        return (x * c).astype(np.float32) + (sw * s).astype(np.float32)
+
+    q = rot(qkv[:hq * 128].reshape(hq, 128))
+    k_new = rot(qkv[hq * 128:(hq + hkv) * 128].reshape(hkv, 128))
+    v_new = qkv[(hq + hkv) * 128:].reshape(hkv, 128)
+    k_ref, v_ref = k.copy(), v.copy()
+    k_ref[:, pos], v_ref[:, pos] = k_new, v_new
+    ref = np.empty((hq, 128))
+    for h in range(hq):
+        kh = h // (hq // hkv)
+        sc = k_ref[kh, :pos + 1].astype(np.float64) @ q[h] / np.sqrt(128.0)
+        p = np.exp(sc - sc.max())
+        ref[h] = (p / p.sum()) @ v_ref[kh, :pos + 1]
+    for _ in range(2):  # the arrival counters are back at zero after a call
+        kd, vd = torch.from_numpy(k).to(dev), torch.from_numpy(v).to(dev)
+        _lib.check(L.q8lin_rope_attention_decode(_p(qkv_d), _p(pos_d), _p(cos_d), _p(sin_d), _p(kd), _p(vd), hq, hkv,
+                                                 128, max_t, _p(ws), ws.numel(), _p(out), _s()))
+        torch.cuda.synchronize()
+        assert np.max(np.abs(out.cpu().numpy() - ref)) <= 2e-5 * np.max(np.abs(ref))
+        assert np.array_equal(kd.cpu().numpy(), k_ref) and np.array_equal(vd.cpu().numpy(), v_ref)
+    st = ctypes.c_uint32(0)
+    _lib.check(L.q8lin_fault_status(torch.cuda.current_device(), ctypes.byref(st), 1))
+    assert st.value == 0
+
+
 def test_argmax_picks_lowest_index_of_the_max_and_advances_pos(cuda_device):
     L, dev = _lib.lib(), cuda_device
     logits = torch.randn(73448, device=dev)
@@ -129,8 +174,8 @@ def _rel(a, b):
     return float(np.linalg.norm(a.astype(np.float64) - b) / np.linalg.norm(b))
 
 
-@pytest.mark.parametrize("heads,kv_heads", [(2, 2), (4, 2)])
-def test_decoder_steps_match_reference(oracle_lib, cuda_device, heads, kv_heads):
+@pytest.mark.parametrize("heads,kv_heads,fused", [(2, 2, True), (4, 2, True), (4, 2, False)])
+def test_decoder_steps_match_reference(oracle_lib, cuda_device, heads, kv_heads, fused):
     from oracle.decoder_ref import DecoderRef
 
     cfg, w = _tiny(heads, kv_heads, 10 + heads)
@@ -144,7 +189,7 @@ def test_decoder_steps_match_reference(oracle_lib, cuda_device, heads, kv_heads)
         if pos < len(prefix):
             tok = prefix[pos]
             dec.token.fill_(tok)
-        dec.step()
+        dec.step(fused=fused)
         lr = ref.step(tok, pos)
         lg = dec.logits.cpu().numpy()
         assert _rel(lg, lr) <= LOGITS_REL_L2, f"step {pos}"
@@ -152,6 +197,43 @@ def test_decoder_steps_match_reference(oracle_lib, cuda_device, heads, kv_heads)
         assert nxt == int(np.argmax(lr)), f"step {pos}"
         assert int(dec.pos.item()) == pos + 1
         tok = nxt
+
+
+def test_fused_forward_prologues_and_residual(oracle_lib, cuda_device):
+    """q8lin_forward_fused against the unfused kernels it replaces."""
+    from talechime_b200.tp_mlp import swiglu
+
+    rng = np.random.default_rng(50)
+    dev = cuda_device
+    k, n = 2048, 300
+    w = synth.q8_0_blocks(rng, n, k)
+    q = QMatMul.from_gguf_blocks(w, n, k, device=dev)
+    x = torch.from_numpy(rng.standard_normal(k).astype(np.float32)).to(dev)
+    nw = torch.from_numpy(rng.uniform(0.5, 1.5, k).astype(np.float32)).to(dev)
+    res = torch.from_numpy(rng.standard_normal(n).astype(np.float32)).to(dev)
+    L = _lib.lib()
+    # rms_norm prologue + residual
+    y = torch.empty(n, device=dev)
+    q.forward_fused(x, y, QMatMul.PROLOGUE_RMSNORM, nw, 1e-5, residual=res)
+    h = torch.empty(k, device=dev)
+    _lib.check(L.q8lin_rmsnorm(_p(x), _p(nw), 1, k, 1e-5, _p(h), _s()))
+    xn = h.cpu().numpy()
+    ref = oracle_lib.matmul(xn[None, :], w, n)[0] + res.cpu().numpy()
+    assert _rel(y.cpu().numpy(), ref) <= LOGITS_REL_L2
+    # plain + in-place residual
+    y2 = res.clone()
+    q.forward_fused(h, y2, residual=y2)
+    assert _rel(y2.cpu().numpy(), ref) <= 1e-5
+    # SwiGLU prologue
+    gu = torch.from_numpy(rng.standard_normal(2 * k).astype(np.float32)).to(dev)
+    y3 = torch.empty(n, device=dev)
+    q.forward_fused(gu, y3, QMatMul.PROLOGUE_SWIGLU)
+    hs = swiglu(gu.view(1, -1), k).cpu().numpy()
+    assert _rel(y3.cpu().numpy(), oracle_lib.matmul(hs, w, n)[0]) <= 1e-5
+    with pytest.raises(_lib.Q8LinError):
+        q.forward_fused(torch.empty((2, k), device=dev), torch.empty((2, n), device=dev))  # one row only
+    x2, y4 = torch.empty((2, k), device=dev), torch.empty((2, n), device=dev)
+    assert L.q8lin_forward_fused(q.handle, _p(x2), _p(y4), 2, 0, None, 1e-5, None, _s()) == _lib.ERR_SHAPE
 
 
 def test_decoder_graph_replay_matches_eager(cuda_device):
