@@ -46,7 +46,10 @@ enum q8lin_status {
   Q8LIN_ERR_NCCL = 5,             /* a collective failed (tensor-parallel entry points) */
   Q8LIN_ERR_OUT_OF_MEMORY = 6,
   Q8LIN_ERR_DEVICE = 7,           /* not a compute-capability 10.0 GPU, or wrong device */
-  Q8LIN_ERR_WORKSPACE = 8         /* caller workspace smaller than q8lin_workspace_size */
+  Q8LIN_ERR_WORKSPACE = 8,        /* caller workspace smaller than q8lin_workspace_size */
+  Q8LIN_ERR_FORMAT = 9,           /* malformed GGUF file, or a value/tensor of the wrong type */
+  Q8LIN_ERR_IO = 10,              /* a file could not be opened or mapped */
+  Q8LIN_ERR_NOT_FOUND = 11        /* GGUF metadata key or tensor name not present */
 };
 
 /* Library version (Q8LIN_VERSION). */
@@ -195,6 +198,61 @@ size_t q8lin_argmax_workspace_size(void);
  * workspace must be zero-filled once before first use. */
 int q8lin_argmax(const float* logits, int64_t n, void* workspace, size_t workspace_bytes, int32_t* token, int32_t* pos,
                  q8lin_stream_t stream);
+
+/*
+ * GGUF reader (versions 2 and 3): replaces candle's gguf_file::Content as used by
+ * Weights::open / ::linear / ::value (crates/voxcpm/src/weights.rs:31-41, :96-115,
+ * :117-137).  The file is mapped read-only; names and string values returned point into
+ * the handle and stay valid until q8lin_gguf_close.  Tensor dims are GGUF `ne` order
+ * (ne[0] contiguous; a [N out, K in] linear has ne = {K, N}); unused dims are 1.
+ */
+typedef struct q8lin_gguf q8lin_gguf;
+
+enum q8lin_ggml_type {
+  Q8LIN_GGML_F32 = 0,
+  Q8LIN_GGML_F16 = 1,
+  Q8LIN_GGML_Q8_0 = 8,
+  Q8LIN_GGML_BF16 = 30
+};
+
+/* GGUF metadata value types (published numbering). */
+enum q8lin_gguf_value_type {
+  Q8LIN_GGUF_U8 = 0, Q8LIN_GGUF_I8 = 1, Q8LIN_GGUF_U16 = 2, Q8LIN_GGUF_I16 = 3,
+  Q8LIN_GGUF_U32 = 4, Q8LIN_GGUF_I32 = 5, Q8LIN_GGUF_F32 = 6, Q8LIN_GGUF_BOOL = 7,
+  Q8LIN_GGUF_STRING = 8, Q8LIN_GGUF_ARRAY = 9, Q8LIN_GGUF_U64 = 10, Q8LIN_GGUF_I64 = 11,
+  Q8LIN_GGUF_F64 = 12
+};
+
+int q8lin_gguf_open(const char* path, q8lin_gguf** out);
+int q8lin_gguf_close(q8lin_gguf* g);
+int q8lin_gguf_version(const q8lin_gguf* g, uint32_t* version);
+int64_t q8lin_gguf_tensor_count(const q8lin_gguf* g);   /* -1 for a null handle */
+int64_t q8lin_gguf_metadata_count(const q8lin_gguf* g); /* -1 for a null handle */
+/* Index of a tensor by name; Q8LIN_ERR_NOT_FOUND if absent. */
+int q8lin_gguf_find_tensor(const q8lin_gguf* g, const char* name, int64_t* index);
+/* Any output pointer may be NULL.  dims receives 4 values.  nbytes is 0 for a ggml type
+ * the reader cannot size (its bytes cannot be read). */
+int q8lin_gguf_tensor_info(const q8lin_gguf* g, int64_t index, const char** name, uint32_t* ggml_type,
+                           uint32_t* n_dims, int64_t* dims, uint64_t* nbytes);
+/* Host pointer to a tensor's bytes inside the mapping. */
+int q8lin_gguf_tensor_data(const q8lin_gguf* g, int64_t index, const void** data, uint64_t* nbytes);
+int q8lin_gguf_metadata_type(const q8lin_gguf* g, const char* key, uint32_t* value_type);
+/* Typed getters: _u32 accepts a U32 value only (like Value::to_u32); _i64 any integer or
+ * bool; _f64 any number; Q8LIN_ERR_NOT_FOUND if the key is absent, Q8LIN_ERR_FORMAT if
+ * the type does not match. */
+int q8lin_gguf_metadata_u32(const q8lin_gguf* g, const char* key, uint32_t* value);
+int q8lin_gguf_metadata_i64(const q8lin_gguf* g, const char* key, int64_t* value);
+int q8lin_gguf_metadata_f64(const q8lin_gguf* g, const char* key, double* value);
+/* String bytes (not NUL-terminated) and their length. */
+int q8lin_gguf_metadata_string(const q8lin_gguf* g, const char* key, const char** data, uint64_t* len);
+/* Array element type and count; data / nbytes (may be NULL) give the raw element bytes
+ * (for string or nested arrays, their serialized form). */
+int q8lin_gguf_metadata_array(const q8lin_gguf* g, const char* key, uint32_t* elem_type, uint64_t* count,
+                              const void** data, uint64_t* nbytes);
+/* q8lin_weight_create from a Q8_0 matrix tensor of the file (Weights::linear's
+ * QMatMul::QTensor branch, weights.rs:100-104); Q8LIN_ERR_FORMAT for other types. */
+int q8lin_gguf_weight_create(const q8lin_gguf* g, const char* tensor_name, int device, q8lin_stream_t stream,
+                             q8lin_weight** out);
 
 #ifdef __cplusplus
 }

@@ -12,6 +12,7 @@ The arithmetic is in ``libq8lin.so`` (C ABI in include/q8lin.h); build it with
 ``python -m talechime_b200.build``.
 """
 from ._lib import Q8LinError
+from .gguf import GGUFFile
 from .qmatmul import Linear, QMatMul, quantize_rows
 
-__all__ = ["QMatMul", "Linear", "Q8LinError", "quantize_rows"]
+__all__ = ["QMatMul", "Linear", "Q8LinError", "quantize_rows", "GGUFFile"]

@@ -22,6 +22,9 @@ ERR_NCCL = 5
 ERR_OUT_OF_MEMORY = 6
 ERR_DEVICE = 7
 ERR_WORKSPACE = 8
+ERR_FORMAT = 9
+ERR_IO = 10
+ERR_NOT_FOUND = 11
 
 # Every symbol the header declares, with (restype, argtypes).
 _c_p = ctypes.c_void_p
@@ -58,6 +61,26 @@ SIGNATURES = {
     "q8lin_rope_attention_decode": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_int32, ctypes.c_int32,
                                                    ctypes.c_int32, ctypes.c_int32, _c_p, ctypes.c_size_t, _c_p, _c_p]),
     "q8lin_add": (ctypes.c_int, [_c_p, _c_p, _i64, _c_p]),
+    "q8lin_gguf_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_c_p)]),
+    "q8lin_gguf_close": (ctypes.c_int, [_c_p]),
+    "q8lin_gguf_version": (ctypes.c_int, [_c_p, ctypes.POINTER(ctypes.c_uint32)]),
+    "q8lin_gguf_tensor_count": (_i64, [_c_p]),
+    "q8lin_gguf_metadata_count": (_i64, [_c_p]),
+    "q8lin_gguf_find_tensor": (ctypes.c_int, [_c_p, ctypes.c_char_p, ctypes.POINTER(_i64)]),
+    "q8lin_gguf_tensor_info": (ctypes.c_int, [_c_p, _i64, ctypes.POINTER(ctypes.c_char_p),
+                                              ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32),
+                                              ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_uint64)]),
+    "q8lin_gguf_tensor_data": (ctypes.c_int, [_c_p, _i64, ctypes.POINTER(_c_p), ctypes.POINTER(ctypes.c_uint64)]),
+    "q8lin_gguf_metadata_type": (ctypes.c_int, [_c_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32)]),
+    "q8lin_gguf_metadata_u32": (ctypes.c_int, [_c_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32)]),
+    "q8lin_gguf_metadata_i64": (ctypes.c_int, [_c_p, ctypes.c_char_p, ctypes.POINTER(_i64)]),
+    "q8lin_gguf_metadata_f64": (ctypes.c_int, [_c_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
+    "q8lin_gguf_metadata_string": (ctypes.c_int, [_c_p, ctypes.c_char_p, ctypes.POINTER(_c_p),
+                                                  ctypes.POINTER(ctypes.c_uint64)]),
+    "q8lin_gguf_metadata_array": (ctypes.c_int, [_c_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32),
+                                                 ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_c_p),
+                                                 ctypes.POINTER(ctypes.c_uint64)]),
+    "q8lin_gguf_weight_create": (ctypes.c_int, [_c_p, ctypes.c_char_p, ctypes.c_int, _c_p, ctypes.POINTER(_c_p)]),
     "q8lin_argmax_workspace_size": (ctypes.c_size_t, []),
     "q8lin_argmax": (ctypes.c_int, [_c_p, _i64, _c_p, ctypes.c_size_t, _c_p, _c_p, _c_p]),
 }

@@ -19,7 +19,8 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libq8lin.so")
 OBJDIR = os.path.join(PKG, "_build")
 
-SOURCES = ["abi.cu", "layout.cu", "gemv.cu", "gemm_simt.cu", "gemm_tc.cu", "noalloc.cu", "mlp.cu", "gemm_skinny.cu", "decoder.cu"]
+SOURCES = ["abi.cu", "layout.cu", "gemv.cu", "gemm_simt.cu", "gemm_tc.cu", "noalloc.cu", "mlp.cu", "gemm_skinny.cu", "decoder.cu",
+           "gguf.cpp"]
 HEADERS = ["common.cuh", "internal.h"]
 
 NVCC_FLAGS = [
@@ -52,7 +53,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     objs = []
     for src in SOURCES:
         path = os.path.join(CSRC, src)
-        obj = os.path.join(OBJDIR, src.replace(".cu", ".o"))
+        obj = os.path.join(OBJDIR, os.path.splitext(src)[0] + ".o")
         objs.append(obj)
         if force or _stale(obj, [path] + headers):
             cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC, "-c", path, "-o", obj]

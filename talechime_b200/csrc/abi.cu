@@ -165,6 +165,9 @@ const char* q8lin_status_string(int status) {
     case Q8LIN_ERR_OUT_OF_MEMORY: return "Q8LIN_ERR_OUT_OF_MEMORY";
     case Q8LIN_ERR_DEVICE: return "Q8LIN_ERR_DEVICE";
     case Q8LIN_ERR_WORKSPACE: return "Q8LIN_ERR_WORKSPACE";
+    case Q8LIN_ERR_FORMAT: return "Q8LIN_ERR_FORMAT";
+    case Q8LIN_ERR_IO: return "Q8LIN_ERR_IO";
+    case Q8LIN_ERR_NOT_FOUND: return "Q8LIN_ERR_NOT_FOUND";
     default: return "Q8LIN_ERR_UNKNOWN";
   }
 }

@@ -59,8 +59,80 @@ def rope_tables(cfg: DecoderConfig, factors: Optional[np.ndarray] = None) -> tup
     return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
 
 
+# GGUF metadata the reference checks before loading the BaseLM (crates/voxcpm/src/model.rs:119-133).
+VOXCPM_BASELM_EXPECT = {"embedding_length": 2048, "block_count": 28, "feed_forward_length": 6144,
+                        "vocab_size": 73448, "attention.head_count": 16, "attention.head_count_kv": 2,
+                        "attention.key_length": 128, "attention.value_length": 128}
+
+
+def config_from_gguf(g, max_t: int = 640, arch: Optional[str] = None) -> DecoderConfig:
+    """DecoderConfig from a GGUF file's `{arch}.*` metadata (general.architecture when
+    `arch` is None); eps and RoPE theta are the reference's constants
+    (transformer.rs:49-51,104)."""
+    arch = arch or g.value("general.architecture")
+    u = lambda name: g.to_u32(f"{arch}.{name}")
+    heads = u("attention.head_count")
+    hidden = u("embedding_length")
+    return DecoderConfig(hidden=hidden, layers=u("block_count"), heads=heads,
+                         kv_heads=u("attention.head_count_kv"), head_dim=u("attention.key_length"),
+                         inter=u("feed_forward_length"), vocab=u("vocab_size"), max_t=max_t)
+
+
+def weights_from_gguf(g, cfg: DecoderConfig, prefix: str = "") -> tuple[dict, Optional[np.ndarray]]:
+    """The decoder's weight dict from GGUF tensors with the reference's names
+    (transformer.rs:78-88: {prefix}blk.{i}.attn_norm / attn_q / attn_k / attn_v /
+    attn_output / ffn_norm / ffn_gate / ffn_up / ffn_down; model.rs:135-141:
+    token_embd, output_norm, rope_factors_short).  q|k|v and gate|up are fused by
+    concatenating their Q8_0 block rows (no re-quantization); the LM head is
+    `output.weight`, or the embedding when the file ties them.  Returns (weights,
+    rope_factors or None)."""
+    def blocks(name, rows, k):
+        b = g.q8_0_blocks(name)
+        if b.shape != (rows, k // 32 * 34):
+            raise _lib.Q8LinError(_lib.ERR_SHAPE, f"tensor '{name}' is {b.shape[0]} x {b.shape[1] // 34 * 32}, "
+                                                  f"expected {rows} x {k}")
+        return b
+
+    H, D = cfg.hidden, cfg.head_dim
+    layers = []
+    for i in range(cfg.layers):
+        p = f"{prefix}blk.{i}"
+        layers.append({
+            "attn_norm": g.tensor(f"{p}.attn_norm.weight").reshape(-1),
+            "qkv": np.concatenate([blocks(f"{p}.attn_q.weight", cfg.heads * D, H),
+                                   blocks(f"{p}.attn_k.weight", cfg.kv_heads * D, H),
+                                   blocks(f"{p}.attn_v.weight", cfg.kv_heads * D, H)]),
+            "o": blocks(f"{p}.attn_output.weight", H, cfg.heads * D),
+            "ffn_norm": g.tensor(f"{p}.ffn_norm.weight").reshape(-1),
+            "gate_up": np.concatenate([blocks(f"{p}.ffn_gate.weight", cfg.inter, H),
+                                       blocks(f"{p}.ffn_up.weight", cfg.inter, H)]),
+            "down": blocks(f"{p}.ffn_down.weight", H, cfg.inter),
+        })
+    embd = blocks("token_embd.weight", cfg.vocab, H)
+    head = blocks("output.weight", cfg.vocab, H) if "output.weight" in g else embd
+    factors = g.tensor("rope_factors_short.weight").reshape(-1) if "rope_factors_short.weight" in g else None
+    return {"token_embd": embd, "output": head, "output_norm": g.tensor("output_norm.weight").reshape(-1),
+            "layers": layers}, factors
+
+
 class Q8Decoder:
     """Weights, KV cache and step buffers of one decoder on one GPU."""
+
+    @classmethod
+    def from_gguf(cls, path: str, device: torch.device | int | str = 0, max_t: int = 640,
+                  expect: Optional[dict] = None, arch: Optional[str] = None) -> "Q8Decoder":
+        """Load a decoder from a GGUF file (Model::load_files_with_cancel's BaseLM half,
+        crates/voxcpm/src/model.rs:118-145).  `expect` maps `{arch}.`-relative metadata
+        keys to required u32 values (VOXCPM_BASELM_EXPECT for the production file)."""
+        from .gguf import GGUFFile
+
+        with GGUFFile(path) as g:
+            arch = arch or g.value("general.architecture")
+            for name, val in (expect or {}).items():
+                g.expect_u32(f"{arch}.{name}", val)
+            cfg = config_from_gguf(g, max_t=max_t, arch=arch)
+            weights, factors = weights_from_gguf(g, cfg)
+        return cls(cfg, weights, device=device, rope_factors=factors)
 
     def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | int | str = 0,
                  rope_factors: Optional[np.ndarray] = None):
