@@ -126,7 +126,8 @@ int q8lin_forward_noalloc(const q8lin_weight* w, const float* x, float* y, int64
 /*
  * Device-side fault word of `device` (bit 0: a tensor-core kernel's bounded wait ran
  * out, bit 1: the M = 1 streaming GEMV's, bit 2: the small-batch int8 kernel's, bit 3:
- * the fused attention's; the kernel returned early and its output is invalid).  Reads it with a
+ * the fused attention's, bit 4: the persistent decode step's; the kernel returned early
+ * and its output is invalid).  Reads it with a
  * device synchronisation; `clear` resets it.  No counterpart in the reference (candle's
  * kernels have no bounded waits); this is the library's failure-detection hook.
  */
@@ -184,13 +185,13 @@ size_t q8lin_attention_workspace_size(int32_t hq, int32_t max_t);
 int q8lin_attention_decode(const float* q, const float* k_cache, const float* v_cache, const int32_t* pos,
                            int32_t hq, int32_t hkv, int32_t d, int32_t max_t, void* workspace, size_t workspace_bytes,
                            float* out, q8lin_stream_t stream);
-size_t q8lin_rope_attention_workspace_size(int32_t hq, int32_t max_t);
 /* RoPE + KV append + attention in one launch: rotates q and the current k of qkv at *pos,
  * appends k and v to the caches at row *pos and writes out[hq][d] = softmax(q K^T /
- * sqrt(d)) V over rows [0, *pos]; d = 128.  Workspace zero-filled once before first use. */
+ * sqrt(d)) V over rows [0, *pos]; d = 128.  One cluster of 8 CTAs per q head; no
+ * workspace. */
 int q8lin_rope_attention_decode(const float* qkv, const int32_t* pos, const float* cos_t, const float* sin_t,
                                 float* k_cache, float* v_cache, int32_t hq, int32_t hkv, int32_t d, int32_t max_t,
-                                void* workspace, size_t workspace_bytes, float* out, q8lin_stream_t stream);
+                                float* out, q8lin_stream_t stream);
 /* x[0..n) += y[0..n). */
 int q8lin_add(float* x, const float* y, int64_t n, q8lin_stream_t stream);
 size_t q8lin_argmax_workspace_size(void);
@@ -198,6 +199,53 @@ size_t q8lin_argmax_workspace_size(void);
  * workspace must be zero-filled once before first use. */
 int q8lin_argmax(const float* logits, int64_t n, void* workspace, size_t workspace_bytes, int32_t* token, int32_t* pos,
                  q8lin_stream_t stream);
+
+/*
+ * Persistent decode step: a program of operations run by ONE cooperative launch (one
+ * CTA per SM).  The weights of every GEMV stream through each SM's shared-memory ring
+ * ahead of the data; operation i starts when every CTA has finished operation i - 1.
+ * Semantics per operation equal the multi-launch entry points:
+ *   GEMV       y = [residual +] W . prologue(x), M = 1 (q8lin_forward_fused), K <= 8192;
+ *              epilogue Q8LIN_EPILOGUE_SWIGLU: W holds [gate | up] rows (N = 2I) and
+ *              y[i] = silu(gate_i) * up_i for i < I (K <= 2048, no residual);
+ *              argmax != 0 records row maxima for a following ARGMAX op;
+ *   ATTENTION  q8lin_rope_attention_decode on x = qkv at *pos into y [hq * head_dim];
+ *   EMBED      y[0..K) = dequantized row *token of the weight (q8lin_embed_rows);
+ *   ARGMAX     *token = argmax of the preceding GEMV's output, *pos += 1 (q8lin_argmax).
+ * Pointers stay owned by the caller and must outlive the step.  q8lin_step_run is
+ * stream-ordered, allocates nothing and may be captured in a CUDA graph; a step object
+ * serves one stream at a time.  Fault word bit 4: a bounded wait of the step timed out.
+ */
+typedef struct q8lin_step q8lin_step;
+
+enum q8lin_op_kind { Q8LIN_OP_GEMV = 0, Q8LIN_OP_ATTENTION = 1, Q8LIN_OP_EMBED = 2, Q8LIN_OP_ARGMAX = 3 };
+#define Q8LIN_PROLOGUE_NONE 0
+#define Q8LIN_PROLOGUE_RMSNORM 1
+#define Q8LIN_PROLOGUE_SWIGLU 2
+#define Q8LIN_EPILOGUE_NONE 0
+#define Q8LIN_EPILOGUE_SWIGLU 1
+
+typedef struct q8lin_op {
+  int32_t kind;                /* q8lin_op_kind */
+  int32_t prologue;            /* GEMV: Q8LIN_PROLOGUE_* */
+  int32_t epilogue;            /* GEMV: Q8LIN_EPILOGUE_* */
+  int32_t argmax;              /* GEMV: feed the following ARGMAX op */
+  const q8lin_weight* weight;  /* GEMV, EMBED */
+  const float* x;              /* GEMV input (2K values for the SwiGLU prologue); ATTENTION: qkv */
+  float* y;                    /* GEMV output; EMBED output [K]; ATTENTION output */
+  const float* residual;       /* GEMV: added to y (may alias y) */
+  const float* norm_weight;    /* GEMV RMSNORM: [K] */
+  float* k_cache;              /* ATTENTION: [hkv][max_t][head_dim] */
+  float* v_cache;
+  const float* cos_t;          /* ATTENTION: [max_t][head_dim / 2] */
+  const float* sin_t;
+  float eps;                   /* GEMV RMSNORM */
+  int32_t hq, hkv, head_dim, max_t;
+} q8lin_op;
+
+int q8lin_step_create(const q8lin_op* ops, int32_t nops, int32_t* pos, int32_t* token, int device, q8lin_step** out);
+int q8lin_step_run(q8lin_step* step, q8lin_stream_t stream);
+int q8lin_step_destroy(q8lin_step* step);
 
 /*
  * GGUF reader (versions 2 and 3): replaces candle's gguf_file::Content as used by

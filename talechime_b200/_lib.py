@@ -26,6 +26,20 @@ ERR_FORMAT = 9
 ERR_IO = 10
 ERR_NOT_FOUND = 11
 
+class Op(ctypes.Structure):
+    """struct q8lin_op (one operation of a persistent decode step)."""
+    _fields_ = [("kind", ctypes.c_int32), ("prologue", ctypes.c_int32), ("epilogue", ctypes.c_int32),
+                ("argmax", ctypes.c_int32), ("weight", ctypes.c_void_p), ("x", ctypes.c_void_p),
+                ("y", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("norm_weight", ctypes.c_void_p),
+                ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p), ("cos_t", ctypes.c_void_p),
+                ("sin_t", ctypes.c_void_p), ("eps", ctypes.c_float), ("hq", ctypes.c_int32),
+                ("hkv", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("max_t", ctypes.c_int32)]
+
+
+OP_GEMV, OP_ATTENTION, OP_EMBED, OP_ARGMAX = 0, 1, 2, 3
+PROLOGUE_NONE, PROLOGUE_RMSNORM, PROLOGUE_SWIGLU = 0, 1, 2
+EPILOGUE_NONE, EPILOGUE_SWIGLU = 0, 1
+
 # Every symbol the header declares, with (restype, argtypes).
 _c_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -57,10 +71,13 @@ SIGNATURES = {
     "q8lin_attention_workspace_size": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32]),
     "q8lin_attention_decode": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, ctypes.c_int32, ctypes.c_int32,
                                               ctypes.c_int32, ctypes.c_int32, _c_p, ctypes.c_size_t, _c_p, _c_p]),
-    "q8lin_rope_attention_workspace_size": (ctypes.c_size_t, [ctypes.c_int32, ctypes.c_int32]),
     "q8lin_rope_attention_decode": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_int32, ctypes.c_int32,
-                                                   ctypes.c_int32, ctypes.c_int32, _c_p, ctypes.c_size_t, _c_p, _c_p]),
+                                                   ctypes.c_int32, ctypes.c_int32, _c_p, _c_p]),
     "q8lin_add": (ctypes.c_int, [_c_p, _c_p, _i64, _c_p]),
+    "q8lin_step_create": (ctypes.c_int, [ctypes.POINTER(Op), ctypes.c_int32, _c_p, _c_p, ctypes.c_int,
+                                         ctypes.POINTER(_c_p)]),
+    "q8lin_step_run": (ctypes.c_int, [_c_p, _c_p]),
+    "q8lin_step_destroy": (ctypes.c_int, [_c_p]),
     "q8lin_gguf_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_c_p)]),
     "q8lin_gguf_close": (ctypes.c_int, [_c_p]),
     "q8lin_gguf_version": (ctypes.c_int, [_c_p, ctypes.POINTER(ctypes.c_uint32)]),

@@ -8,6 +8,7 @@
 #include <mutex>
 #include <string>
 #include <utility>
+#include <vector>
 
 #include "common.cuh"
 #include "internal.h"
@@ -354,13 +355,14 @@ int q8lin_fault_status(int device, uint32_t* flags, int clear) {
   int st = check_device(device);
   if (st != Q8LIN_OK) return st;
   DeviceGuard guard(device);
-  unsigned int f = 0, g = 0, h = 0, a = 0;
+  unsigned int f = 0, g = 0, h = 0, a = 0, p = 0;
   cudaError_t e = read_tc_fault(&f, clear != 0);
   if (e == cudaSuccess) e = read_gemv_fault(&g, clear != 0);
   if (e == cudaSuccess) e = read_skinny_fault(&h, clear != 0);
   if (e == cudaSuccess) e = read_attention_fault(&a, clear != 0);
+  if (e == cudaSuccess) e = read_step_fault(&p, clear != 0);
   if (e != cudaSuccess) return cuda_fail(e, "read fault word");
-  *flags = f | g | h | a;
+  *flags = f | g | h | a | p;
   return Q8LIN_OK;
 }
 
@@ -471,26 +473,19 @@ int q8lin_attention_decode(const float* q, const float* k_cache, const float* v_
   return Q8LIN_OK;
 }
 
-size_t q8lin_rope_attention_workspace_size(int32_t hq, int32_t max_t) {
-  if (hq <= 0 || max_t <= 0) return 0;
-  return rope_attention_workspace_bytes(hq, max_t);
-}
-
 int q8lin_rope_attention_decode(const float* qkv, const int32_t* pos, const float* cos_t, const float* sin_t,
                                 float* k_cache, float* v_cache, int32_t hq, int32_t hkv, int32_t d, int32_t max_t,
-                                void* workspace, size_t workspace_bytes, float* out, q8lin_stream_t stream) {
+                                float* out, q8lin_stream_t stream) {
   if (d != 128) return fail(Q8LIN_ERR_SHAPE, "rope_attention_decode supports head width 128");
-  if (hq <= 0 || hkv <= 0 || hq % hkv || max_t <= 0)
+  if (hq <= 0 || hkv <= 0 || hq % hkv || max_t <= 0 || hq > 65535)
     return fail(Q8LIN_ERR_SHAPE, "attention needs hq a positive multiple of hkv and max_t > 0");
-  if (!qkv || !pos || !cos_t || !sin_t || !k_cache || !v_cache || !workspace || !out)
+  if (!qkv || !pos || !cos_t || !sin_t || !k_cache || !v_cache || !out)
     return fail(Q8LIN_ERR_INVALID_ARGUMENT, "rope_attention pointers must be non-null device pointers");
   if (!aligned16(k_cache) || !aligned16(v_cache)) return fail(Q8LIN_ERR_ALIGNMENT, "the caches must be 16-byte aligned");
-  if (workspace_bytes < rope_attention_workspace_bytes(hq, max_t))
-    return fail(Q8LIN_ERR_WORKSPACE, "attention workspace too small (see q8lin_rope_attention_workspace_size)");
   int device = 0;
   cudaGetDevice(&device);
-  cudaError_t e = launch_rope_attention(qkv, pos, cos_t, sin_t, k_cache, v_cache, hq, hkv, max_t, workspace, out,
-                                        device, reinterpret_cast<cudaStream_t>(stream));
+  cudaError_t e = launch_rope_attention(qkv, pos, cos_t, sin_t, k_cache, v_cache, hq, hkv, max_t, out, device,
+                                        reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rope_attention launch");
   return Q8LIN_OK;
 }
@@ -514,6 +509,179 @@ int q8lin_argmax(const float* logits, int64_t n, void* workspace, size_t workspa
     return fail(Q8LIN_ERR_WORKSPACE, "argmax workspace too small (see q8lin_argmax_workspace_size)");
   cudaError_t e = launch_argmax(logits, (int)n, workspace, token, pos, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "argmax launch");
+  return Q8LIN_OK;
+}
+
+}  // extern "C"
+
+struct q8lin_step {
+  int device = -1;
+  int nops = 0;
+  int grid = 0;
+  q8lin::StepOp* ops = nullptr;  // device copy of the program
+  unsigned* done = nullptr;      // [nops + 1] arrival counters
+  float* attn_part = nullptr;    // [hq][splits][132]
+  unsigned* head_cnt = nullptr;  // [hq]
+  float* am_gv = nullptr;        // [grid]
+  int* am_gi = nullptr;          // [grid]
+  int32_t* pos = nullptr;
+  int32_t* token = nullptr;
+};
+
+namespace q8lin {
+namespace {
+
+void step_free(q8lin_step* st) {
+  if (!st) return;
+  cudaFree(st->ops);
+  cudaFree(st->done);
+  cudaFree(st->attn_part);
+  cudaFree(st->head_cnt);
+  cudaFree(st->am_gv);
+  cudaFree(st->am_gi);
+  delete st;
+}
+
+int op_fail(int i, const std::string& msg) { return fail(Q8LIN_ERR_INVALID_ARGUMENT, "op " + std::to_string(i) + ": " + msg); }
+
+}  // namespace
+}  // namespace q8lin
+
+extern "C" {
+
+int q8lin_step_create(const q8lin_op* ops, int32_t nops, int32_t* pos, int32_t* token, int device, q8lin_step** out) {
+  if (!out) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "out is null");
+  *out = nullptr;
+  if (!ops || nops <= 0 || nops > 65536) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "ops must hold 1..65536 operations");
+  if (!pos || !token) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "pos and token must be device pointers");
+  int st = check_device(device);
+  if (st != Q8LIN_OK) return st;
+  std::vector<StepOp> dev_ops((size_t)nops);
+  int max_hq = 0;
+  for (int i = 0; i < nops; ++i) {
+    const q8lin_op& o = ops[i];
+    StepOp& d = dev_ops[(size_t)i];
+    d = StepOp();
+    d.kind = o.kind;
+    d.prologue = o.prologue;
+    if (o.kind == Q8LIN_OP_GEMV || o.kind == Q8LIN_OP_EMBED) {
+      const q8lin_weight* w = o.weight;
+      if (!w || !w->packed) return op_fail(i, "needs a weight");
+      if (w->device != device) return fail(Q8LIN_ERR_DEVICE, "op " + std::to_string(i) + ": weight on another device");
+      d.n = (int)w->n;
+      d.k = (int)w->k;
+      d.S = w->row_stride;
+      d.W = w->packed;
+      d.y = o.y;
+      if (!o.y || !aligned16(o.y)) return op_fail(i, "y must be a 16-byte aligned device pointer");
+    }
+    switch (o.kind) {
+      case Q8LIN_OP_GEMV: {
+        if (d.k > kStepMaxK) return fail(Q8LIN_ERR_SHAPE, "op " + std::to_string(i) + ": K beyond 8192");
+        d.rpc = step_rows_per_chunk(d.k);
+        if (d.rpc < 1) return fail(Q8LIN_ERR_SHAPE, "op " + std::to_string(i) + ": row too wide for the ring");
+        if (o.prologue < Q8LIN_PROLOGUE_NONE || o.prologue > Q8LIN_PROLOGUE_SWIGLU) return op_fail(i, "unknown prologue");
+        if (o.epilogue != Q8LIN_EPILOGUE_NONE && o.epilogue != Q8LIN_EPILOGUE_SWIGLU) return op_fail(i, "unknown epilogue");
+        if (!o.x || !aligned16(o.x)) return op_fail(i, "x must be a 16-byte aligned device pointer");
+        if (o.prologue == Q8LIN_PROLOGUE_RMSNORM && (!o.norm_weight || !aligned16(o.norm_weight)))
+          return op_fail(i, "rms_norm needs a 16-byte aligned norm weight");
+        if (o.residual && !aligned16(o.residual)) return op_fail(i, "residual must be 16-byte aligned");
+        if (o.epilogue == Q8LIN_EPILOGUE_SWIGLU) {
+          if (d.n % 2 || d.rpc < 2 || d.k > 2048 || o.residual || o.argmax)
+            return fail(Q8LIN_ERR_SHAPE, "op " + std::to_string(i) +
+                                             ": the SwiGLU epilogue takes [gate | up] rows, K <= 2048, no residual "
+                                             "or argmax");
+        }
+        d.x = o.x;
+        d.residual = o.residual;
+        d.norm_w = o.norm_weight;
+        d.eps = o.eps;
+        d.argmax = o.argmax ? 1 : 0;
+        d.epilogue = o.epilogue;
+        break;
+      }
+      case Q8LIN_OP_ATTENTION: {
+        if (o.head_dim != 128) return fail(Q8LIN_ERR_SHAPE, "op " + std::to_string(i) + ": head width must be 128");
+        if (o.hq <= 0 || o.hkv <= 0 || o.hq % o.hkv || o.max_t <= 0 || o.hq > 4096)
+          return fail(Q8LIN_ERR_SHAPE, "op " + std::to_string(i) + ": needs hq a multiple of hkv");
+        if (!o.x || !o.y || !o.k_cache || !o.v_cache || !o.cos_t || !o.sin_t) return op_fail(i, "attention pointers are null");
+        if (!aligned16(o.x) || !aligned16(o.y) || !aligned16(o.k_cache) || !aligned16(o.v_cache))
+          return fail(Q8LIN_ERR_ALIGNMENT, "op " + std::to_string(i) + ": qkv, output and caches must be 16-byte aligned");
+        d.x = o.x;
+        d.y = o.y;
+        d.hq = o.hq;
+        d.hkv = o.hkv;
+        d.max_t = o.max_t;
+        d.scale = (float)(1.0 / std::sqrt(128.0));
+        d.kc = o.k_cache;
+        d.vc = o.v_cache;
+        d.cos_t = o.cos_t;
+        d.sin_t = o.sin_t;
+        if (o.hq > max_hq) max_hq = o.hq;
+        break;
+      }
+      case Q8LIN_OP_EMBED:
+        break;
+      case Q8LIN_OP_ARGMAX:
+        if (i == 0 || ops[i - 1].kind != Q8LIN_OP_GEMV || !ops[i - 1].argmax)
+          return op_fail(i, "an argmax op follows a GEMV with argmax set");
+        d.n = (int)ops[i - 1].weight->n;
+        break;
+      default:
+        return op_fail(i, "unknown kind");
+    }
+  }
+  DeviceGuard guard(device);
+  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
+  q8lin_step* s = new q8lin_step();
+  s->device = device;
+  s->nops = nops;
+  s->pos = pos;
+  s->token = token;
+  cudaError_t e = step_max_grid(device, &s->grid);
+  if (e == cudaSuccess && s->grid <= 0) {
+    delete s;
+    return fail(Q8LIN_ERR_DEVICE, "the decode-step kernel does not fit on an SM");
+  }
+  if (e == cudaSuccess) e = cudaMalloc(&s->ops, sizeof(StepOp) * (size_t)nops);
+  if (e == cudaSuccess) e = cudaMalloc(&s->done, sizeof(unsigned) * (size_t)(nops + 1));
+  const size_t hq_alloc = (size_t)(max_hq > 0 ? max_hq : 1);
+  if (e == cudaSuccess) e = cudaMalloc(&s->attn_part, sizeof(float) * hq_alloc * step_splits() * 132);
+  if (e == cudaSuccess) e = cudaMalloc(&s->head_cnt, sizeof(unsigned) * hq_alloc);
+  if (e == cudaSuccess) e = cudaMemset(s->head_cnt, 0, sizeof(unsigned) * hq_alloc);
+  if (e == cudaSuccess)
+    for (StepOp& d : dev_ops)
+      if (d.kind == kStepOpAttention) {
+        d.attn_part = s->attn_part;
+        d.head_cnt = s->head_cnt;
+      }
+  if (e == cudaSuccess) e = cudaMalloc(&s->am_gv, sizeof(float) * (size_t)s->grid);
+  if (e == cudaSuccess) e = cudaMalloc(&s->am_gi, sizeof(int) * (size_t)s->grid);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(s->ops, dev_ops.data(), sizeof(StepOp) * (size_t)nops, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(s->done, 0, sizeof(unsigned) * (size_t)(nops + 1));
+  if (e != cudaSuccess) {
+    step_free(s);
+    return cuda_fail(e, "decode-step setup");
+  }
+  *out = s;
+  return Q8LIN_OK;
+}
+
+int q8lin_step_run(q8lin_step* s, q8lin_stream_t stream) {
+  if (!s) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "step is null");
+  DeviceGuard guard(s->device);
+  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaError_t e = launch_decode_step(s->ops, s->nops, s->pos, s->token, s->done, s->am_gv, s->am_gi, s->grid,
+                                     s->device, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "decode-step launch");
+  return Q8LIN_OK;
+}
+
+int q8lin_step_destroy(q8lin_step* s) {
+  if (!s) return Q8LIN_OK;
+  DeviceGuard guard(s->device);
+  step_free(s);
   return Q8LIN_OK;
 }
 

@@ -190,67 +190,108 @@ attention_decode_kernel(const float* __restrict__ q, const float* __restrict__ k
 
 // ---------------------------------------------------------------------------------
 // RoPE + KV append + attention in one kernel (the decode step's attention block).
-// grid (Hq, splits of kRaPositions positions); 256 threads.  A CTA:
-//   * bulk-copies the cached K and V rows [t0, min(t1, pos)) of its kv head into shared
-//     memory (one cp.async.bulk each, mbarrier complete_tx);
-//   * meanwhile rotates q of its head and, if its range holds the current position, k and
-//     v of the current token straight from the qkv projection (so no CTA reads a cache
-//     row another CTA of this launch writes); the first q head of each kv head appends
-//     k and v to the cache;
-//   * scores 4 positions per warp at a time, softmax within the CTA (max, exp, sum), the
-//     weighted sum of V by 256 threads (two position halves per dimension), and writes
-//     its (max, sum, acc[128]) partial; the last CTA of the head merges the partials in
-//     split order and writes the output.
-constexpr int kRaPositions = 64;
+// grid (kRaCluster, Hq) with clusters of kRaCluster CTAs: cluster h serves q head h and
+// its CTAs split the positions [0, pos] evenly (rank r takes [r*per, (r+1)*per) with
+// per = ceil((pos + 1) / kRaCluster)), so the work per CTA follows the current length.
+// A CTA:
+//   * rotates q of its head and, if its range holds the current position, k and v of
+//     the current token straight from the qkv projection (no CTA reads a cache row that
+//     another CTA of this launch writes); the first q head of each kv head appends k
+//     and v to the cache;
+//   * streams its cached K and V rows through a two-slot shared-memory ring of
+//     kRaChunk-row chunks (cp.async.bulk from this GPU's memory, mbarrier complete_tx),
+//     the copy of chunk c + 2 issued as soon as chunk c is consumed;
+//   * per chunk: scores (one warp per 4 positions), a running max / sum / weighted V
+//     sum (online softmax; 256 threads = 128 dims x 2 position halves);
+//   * publishes its (max, sum, acc[128]) in shared memory; after a cluster barrier CTA
+//     rank 0 reads the partials of the cluster through distributed shared memory, merges
+//     them in rank order and writes the output; a second barrier keeps every CTA's
+//     shared memory alive until then.
+constexpr int kRaCluster = 8;
+constexpr int kRaChunk = 32;
 constexpr int kRaThreads = 256;
 constexpr uint32_t kRaSpin = 1u << 24;
 
 __device__ unsigned int g_attn_fault;
 
 struct RaSmem {
-  alignas(16) float k[kRaPositions][128];
-  alignas(16) float v[kRaPositions][128];
+  alignas(16) float k[2][kRaChunk][128];
+  alignas(16) float v[2][kRaChunk][128];
   alignas(16) float q[128];
   alignas(16) float kcur[128];
   alignas(16) float vcur[128];
   alignas(16) float acc2[2][128];
-  float sc[kRaPositions];
-  float red[8];
-  alignas(8) uint64_t bar;
-  int last;
+  alignas(16) float pacc[128];  // this CTA's partial: weighted V sum
+  float sc[kRaChunk];
+  float stat[4];  // running max, running sum, chunk correction, partial max
+  float pl;       // partial sum
+  alignas(8) uint64_t full[2];
 };
+
+__device__ __forceinline__ bool ra_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(bar);
+  for (uint32_t i = 0; i < kRaSpin; ++i) {
+    uint32_t done;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(done) : "r"(a), "r"(parity) : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 __global__ void __launch_bounds__(kRaThreads)
 rope_attention_kernel(const float* __restrict__ qkv, const int* __restrict__ pos_dev, const float* __restrict__ cos_t,
                       const float* __restrict__ sin_t, float* __restrict__ kc, float* __restrict__ vc, int Hq, int Hkv,
-                      int max_t, float scale, float* __restrict__ part, unsigned int* __restrict__ cnt,
-                      float* __restrict__ out) {
+                      int max_t, float scale, float* __restrict__ out) {
   constexpr int D = 128, half = 64;
   extern __shared__ __align__(16) uint8_t ra_raw[];
   RaSmem& sm = *reinterpret_cast<RaSmem*>(ra_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int h = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
+  const int h = blockIdx.y;
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
   const int group = Hq / Hkv, hk = h / group;
-  pdl_wait();
-  const int pos = *pos_dev;
-  const int t0 = split * kRaPositions;
-  const int t1 = min(min(pos + 1, max_t), t0 + kRaPositions);  // never past the cache
-  const int nhere = t1 > t0 ? t1 - t0 : 0;
-  const int rows = min(t1, pos) - t0 > 0 ? min(t1, pos) - t0 : 0;  // cached rows in range
-  const bool cur = t0 <= pos && pos < t1;
-  const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&sm.bar);
-  if (tid == 0 && rows > 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(1) : "memory");
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(&sm.full[i])),
+                   "r"(1) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    const uint32_t bytes = (uint32_t)rows * D * 4;
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
-    const float* ks = kc + ((size_t)hk * max_t + t0) * D;
-    const float* vs = vc + ((size_t)hk * max_t + t0) * D;
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"((uint32_t)__cvta_generic_to_shared(&sm.k[0][0])), "l"(ks), "r"(bytes), "r"(bar) : "memory");
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"((uint32_t)__cvta_generic_to_shared(&sm.v[0][0])), "l"(vs), "r"(bytes), "r"(bar) : "memory");
   }
+  pdl_wait();
+  // the next linear's CTAs may become resident and fill their weight rings meanwhile
+  // (its own dependency wait still covers this grid's writes)
+  pdl_launch_dependents();
+  const int pos = *pos_dev;
+  const int len = pos < 0 ? 0 : min(pos + 1, max_t);  // never past the cache
+  const int per = (len + kRaCluster - 1) / kRaCluster;
+  const int a = min(len, (int)rank * per), b = min(len, a + per);
+  const int nchunks = (b - a + kRaChunk - 1) / kRaChunk;
+  const bool cur = a <= pos && pos < b;
+  const float* kh = kc + (size_t)hk * max_t * D;
+  const float* vh = vc + (size_t)hk * max_t * D;
+  // chunk c holds positions [a + c*kRaChunk, ...); its cached rows are those below pos
+  auto issue = [&](int c) {
+    const int c0 = a + c * kRaChunk, c1 = min(b, c0 + kRaChunk), cached = min(c1, pos) - c0;
+    const int slot = c & 1;
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&sm.full[slot]);
+    const uint32_t bytes = cached > 0 ? (uint32_t)cached * D * 4 : 0u;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
+    if (bytes) {
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   ::"r"((uint32_t)__cvta_generic_to_shared(&sm.k[slot][0][0])), "l"(kh + (size_t)c0 * D),
+                   "r"(bytes), "r"(bar) : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                   ::"r"((uint32_t)__cvta_generic_to_shared(&sm.v[slot][0][0])), "l"(vh + (size_t)c0 * D),
+                   "r"(bytes), "r"(bar) : "memory");
+    }
+  };
+  __syncthreads();  // barrier init visible before any wait
+  if (tid == 0)
+    for (int c = 0; c < min(2, nchunks); ++c) issue(c);
   // rotation x*[cos,cos] + [second,first]*[-sin,sin] at the current position
   if (tid < D && pos >= 0 && pos < max_t) {
     const int j = tid < half ? tid : tid - half;
@@ -271,104 +312,107 @@ rope_attention_kernel(const float* __restrict__ qkv, const int* __restrict__ pos
       }
     }
   }
-  __syncthreads();
-  bool ok = true;
-  if (rows > 0) {
-    ok = false;
-    for (uint32_t i = 0; i < kRaSpin && !ok; ++i) {
-      uint32_t done;
-      asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n selp.u32 %0, 1, 0, p;\n}"
-                   : "=r"(done) : "r"(bar) : "memory");
-      ok = done != 0;
-    }
-    if (!ok && tid == 0) atomicOr(&g_attn_fault, 8u);
+  if (tid == 0) {
+    sm.stat[0] = -INFINITY;
+    sm.stat[1] = 0.0f;
   }
-  // scores: warp w takes positions w*8 .. w*8+7, four at a time
+  __syncthreads();
   const float4 q4 = reinterpret_cast<const float4*>(sm.q)[lane];
-#pragma unroll
-  for (int g = 0; g < 2; ++g) {
+  const int d = tid & 127, hh = tid >> 7;
+  float acc = 0.0f;  // weighted V sum of dimension d over this thread's position half
+  bool ok = true;
+  for (int c = 0; c < nchunks; ++c) {
+    const int slot = c & 1, c0 = a + c * kRaChunk, n = min(b - c0, kRaChunk);
+    if (!ra_wait(&sm.full[slot], (uint32_t)((c >> 1) & 1))) ok = false;
+    // scores: warp w takes positions 4w .. 4w+3 of the chunk
     float s[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int j = warp * 8 + g * 4 + u;
-      const float* krow = (t0 + j == pos) ? sm.kcur : sm.k[j < rows ? j : 0];
+      const int j = warp * 4 + u;
+      const float* krow = (c0 + j == pos) ? sm.kcur : sm.k[slot][j];
       const float4 k4 = reinterpret_cast<const float4*>(krow)[lane];
-      float d = __fmul_rn(q4.x, k4.x);
-      d = __fadd_rn(d, __fmul_rn(q4.y, k4.y));
-      d = __fadd_rn(d, __fmul_rn(q4.z, k4.z));
-      s[u] = __fadd_rn(d, __fmul_rn(q4.w, k4.w));
+      float t = __fmul_rn(q4.x, k4.x);
+      t = __fadd_rn(t, __fmul_rn(q4.y, k4.y));
+      t = __fadd_rn(t, __fmul_rn(q4.z, k4.z));
+      s[u] = __fadd_rn(t, __fmul_rn(q4.w, k4.w));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
       for (int u = 0; u < 4; ++u) s[u] += __shfl_xor_sync(kFull, s[u], o);
-    if (lane == 0)
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = warp * 8 + g * 4 + u;
-        sm.sc[j] = (j < nhere && ok) ? __fmul_rn(s[u], scale) : -INFINITY;
-      }
-  }
-  __syncthreads();
-  // softmax within the CTA: warp 0 reduces max and sum over the 64 scores
-  if (warp == 0) {
-    const float a = sm.sc[lane], b = sm.sc[lane + 32];
-    float mx = fmaxf(a, b);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
-    const float pa = (a == -INFINITY) ? 0.0f : expf(a - mx);
-    const float pb = (b == -INFINITY) ? 0.0f : expf(b - mx);
-    sm.sc[lane] = pa;
-    sm.sc[lane + 32] = pb;
-    const float l = warp_sum(__fadd_rn(pa, pb));
-    if (lane == 0) {
-      sm.red[0] = mx;
-      sm.red[1] = l;
+    if (lane < 4) {
+      const int j = warp * 4 + lane;
+      const float sv = lane == 0 ? s[0] : lane == 1 ? s[1] : lane == 2 ? s[2] : s[3];
+      sm.sc[j] = j < n ? __fmul_rn(sv, scale) : -INFINITY;
     }
-  }
-  __syncthreads();
-  // weighted sum of V: dimension tid % 128, positions half (tid / 128) * 32 .. +32
-  {
-    const int d = tid & 127, hh = tid >> 7;
-    float a = 0.0f;
-    for (int j = hh * 32; j < hh * 32 + 32; ++j) {
-      const float p = sm.sc[j];
-      if (p != 0.0f) {
-        const float vv = (t0 + j == pos) ? sm.vcur[d] : sm.v[j < rows ? j : 0][d];
-        a = __fadd_rn(a, __fmul_rn(p, vv));
+    __syncthreads();
+    if (warp == 0) {  // running max and sum over the chunk's scores
+      const float sv = sm.sc[lane];
+      float mx = sv;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
+      const float m_old = sm.stat[0], m_new = fmaxf(m_old, mx);
+      const float p = (sv == -INFINITY) ? 0.0f : expf(sv - m_new);
+      sm.sc[lane] = p;
+      const float ps = warp_sum(p);
+      if (lane == 0) {
+        const float corr = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
+        sm.stat[0] = m_new;
+        sm.stat[1] = __fadd_rn(__fmul_rn(sm.stat[1], corr), ps);
+        sm.stat[2] = corr;
       }
     }
-    sm.acc2[hh][d] = a;
+    __syncthreads();
+    {
+      float t = 0.0f;
+#pragma unroll 4
+      for (int j = hh * (kRaChunk / 2); j < (hh + 1) * (kRaChunk / 2); ++j) {
+        const float p = sm.sc[j];
+        const float vv = (c0 + j == pos) ? sm.vcur[d] : sm.v[slot][j][d];
+        t = __fadd_rn(t, p != 0.0f ? __fmul_rn(p, vv) : 0.0f);
+      }
+      acc = __fadd_rn(__fmul_rn(acc, sm.stat[2]), t);
+    }
+    __syncthreads();  // slot consumed
+    if (tid == 0 && c + 2 < nchunks) issue(c + 2);
   }
+  if (!ok && tid == 0) atomicOr(&g_attn_fault, 8u);
+  sm.acc2[hh][d] = acc;
   __syncthreads();
-  float* mine = part + ((size_t)h * splits + split) * (2 + D);
-  if (tid < D) mine[2 + tid] = __fadd_rn(sm.acc2[0][tid], sm.acc2[1][tid]);
+  if (tid < D) sm.pacc[tid] = __fadd_rn(sm.acc2[0][tid], sm.acc2[1][tid]);
   if (tid == 0) {
-    mine[0] = nhere > 0 ? sm.red[0] : -INFINITY;
-    mine[1] = nhere > 0 ? sm.red[1] : 0.0f;
+    sm.stat[3] = nchunks > 0 ? sm.stat[0] : -INFINITY;
+    sm.pl = nchunks > 0 ? sm.stat[1] : 0.0f;
   }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) sm.last = (atomicAdd(&cnt[h], 1u) == (unsigned)(splits - 1)) ? 1 : 0;
-  __syncthreads();
-  if (sm.last) {
-    __threadfence();
-    const float* base = part + (size_t)h * splits * (2 + D);
-    if (tid < D) {
-      float M = -INFINITY;
-      for (int s = 0; s < splits; ++s) M = fmaxf(M, base[(size_t)s * (2 + D)]);
-      float L = 0.0f, A = 0.0f;
-      for (int s = 0; s < splits; ++s) {
-        const float ms = base[(size_t)s * (2 + D)];
-        const float f = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-        L = __fadd_rn(L, __fmul_rn(base[(size_t)s * (2 + D) + 1], f));
-        A = __fadd_rn(A, __fmul_rn(base[(size_t)s * (2 + D) + 2 + tid], f));
-      }
-      out[(size_t)h * D + tid] = __fdiv_rn(A, L);
+  cluster_sync();  // partials of every CTA of the cluster written
+  if (rank == 0 && tid < D) {
+    float mr[kRaCluster], lr[kRaCluster], ar[kRaCluster];
+    const uint32_t base_m = (uint32_t)__cvta_generic_to_shared(&sm.stat[3]);
+    const uint32_t base_l = (uint32_t)__cvta_generic_to_shared(&sm.pl);
+    const uint32_t base_a = (uint32_t)__cvta_generic_to_shared(&sm.pacc[tid]);
+#pragma unroll
+    for (int r = 0; r < kRaCluster; ++r) {
+      uint32_t am, al, aa;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(am) : "r"(base_m), "r"(r));
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(al) : "r"(base_l), "r"(r));
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(aa) : "r"(base_a), "r"(r));
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(mr[r]) : "r"(am) : "memory");
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(lr[r]) : "r"(al) : "memory");
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(ar[r]) : "r"(aa) : "memory");
     }
-    if (tid == 0) cnt[h] = 0;
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kRaCluster; ++r) M = fmaxf(M, mr[r]);
+    float L = 0.0f, A = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kRaCluster; ++r) {
+      const float f = (mr[r] == -INFINITY) ? 0.0f : expf(mr[r] - M);
+      L = __fadd_rn(L, __fmul_rn(lr[r], f));
+      A = __fadd_rn(A, __fmul_rn(ar[r], f));
+    }
+    out[(size_t)h * D + tid] = len > 0 ? __fdiv_rn(A, L) : 0.0f;
   }
-  pdl_launch_dependents();
+  cluster_sync();  // rank 0 has read every partial: shared memory may be released
 }
 
 __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, int64_t n) {
@@ -475,18 +519,8 @@ cudaError_t launch_attention_decode(const float* q, const float* kc, const float
   return cudaLaunchKernelEx(&cfg, attention_decode_kernel, q, kc, vc, pos, hq, hkv, max_t, scale, part, cnt, out);
 }
 
-size_t rope_attention_workspace_bytes(int hq, int max_t) {
-  const int splits = (max_t + kRaPositions - 1) / kRaPositions;
-  return ((size_t)hq * splits * (2 + 128) * 4 + 255) / 256 * 256 + ((size_t)hq * 4 + 255) / 256 * 256;
-}
-
 cudaError_t launch_rope_attention(const float* qkv, const int* pos, const float* cos_t, const float* sin_t, float* kc,
-                                  float* vc, int hq, int hkv, int max_t, void* ws, float* out, int device,
-                                  cudaStream_t s) {
-  const int splits = (max_t + kRaPositions - 1) / kRaPositions;
-  float* part = static_cast<float*>(ws);
-  unsigned int* cnt = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(ws) +
-                                                      ((size_t)hq * splits * (2 + 128) * 4 + 255) / 256 * 256);
+                                  float* vc, int hq, int hkv, int max_t, float* out, int device, cudaStream_t s) {
   static int configured[128] = {0};
   const int dev = (device >= 0 && device < 128) ? device : 0;
   if (!configured[dev]) {
@@ -495,12 +529,22 @@ cudaError_t launch_rope_attention(const float* qkv, const int* pos, const float*
     if (e != cudaSuccess) return e;
     configured[dev] = 1;
   }
-  cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = pdl_cfg(dim3((unsigned)hq, (unsigned)splits), dim3(kRaThreads), s, attr);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kRaCluster, (unsigned)hq);
+  cfg.blockDim = dim3(kRaThreads);
   cfg.dynamicSmemBytes = sizeof(RaSmem);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kRaCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   const float scale = (float)(1.0 / std::sqrt(128.0));
-  return cudaLaunchKernelEx(&cfg, rope_attention_kernel, qkv, pos, cos_t, sin_t, kc, vc, hq, hkv, max_t, scale, part,
-                            cnt, out);
+  return cudaLaunchKernelEx(&cfg, rope_attention_kernel, qkv, pos, cos_t, sin_t, kc, vc, hq, hkv, max_t, scale, out);
 }
 
 cudaError_t read_attention_fault(unsigned int* flags, bool clear) {

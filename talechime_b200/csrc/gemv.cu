@@ -273,7 +273,6 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
   }
 
   // ---------------- consumers ----------------
-  pdl_wait();
   {
     // float4 pieces of x, 8 lanes per block; the loads of up to four passes are issued
     // together so K <= 8192 costs one L2 round trip
@@ -281,7 +280,16 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
     constexpr int kQG = 4;
     const int nquads = nb * 8;
     const float4* x4 = reinterpret_cast<const float4*>(x);
-    float4 v[kQG];
+    float4 v[kQG], wn[kQG];
+    if (fz.prologue == kPrologueRmsNorm) {  // the norm weight is constant: load it before the wait
+      const float4* w4 = reinterpret_cast<const float4*>(fz.norm_w);
+#pragma unroll
+      for (int g = 0; g < kQG; ++g) {
+        const int i = g * kT + threadIdx.x;
+        wn[g] = i < nquads ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    pdl_wait();
     if (fz.prologue == kPrologueSwiGLU) {
       // x = [gate | up], K values each: the activation is silu(gate) * up
 #pragma unroll
@@ -320,12 +328,11 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
 #pragma unroll
       for (int i = 0; i < kConsumerWarps; ++i) total += red[i];
       const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)K), fz.eps));
-      const float4* w4 = reinterpret_cast<const float4*>(fz.norm_w);
 #pragma unroll
       for (int g = 0; g < kQG; ++g) {
         const int i = g * kT + threadIdx.x;
         if (i < nquads) {
-          const float4 wv = __ldg(w4 + i);
+          const float4 wv = wn[g];
           v[g] = make_float4(__fmul_rn(__fdiv_rn(v[g].x, m), wv.x), __fmul_rn(__fdiv_rn(v[g].y, m), wv.y),
                              __fmul_rn(__fdiv_rn(v[g].z, m), wv.z), __fmul_rn(__fdiv_rn(v[g].w, m), wv.w));
         }

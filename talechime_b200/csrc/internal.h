@@ -87,12 +87,43 @@ cudaError_t launch_rope_kv(const float* qkv, const int* pos, const float* cos_t,
 size_t attention_workspace_bytes(int hq, int max_t);
 cudaError_t launch_attention_decode(const float* q, const float* kc, const float* vc, const int* pos, int hq,
                                     int hkv, int max_t, void* ws, float* out, cudaStream_t s);
-size_t rope_attention_workspace_bytes(int hq, int max_t);
 cudaError_t launch_rope_attention(const float* qkv, const int* pos, const float* cos_t, const float* sin_t, float* kc,
-                                  float* vc, int hq, int hkv, int max_t, void* ws, float* out, int device,
-                                  cudaStream_t s);
+                                  float* vc, int hq, int hkv, int max_t, float* out, int device, cudaStream_t s);
 cudaError_t read_attention_fault(unsigned int* flags, bool clear);  // bit 3
 cudaError_t launch_add(float* x, const float* y, int64_t n, cudaStream_t s);
+
+// Persistent decode-step kernel (step.cu).
+constexpr int kStepMaxK = 8192;
+enum StepOpKind { kStepOpGemv = 0, kStepOpAttention = 1, kStepOpEmbed = 2, kStepOpArgmax = 3 };
+enum StepPrologue { kStepPrologueNone = 0, kStepPrologueRmsNorm = 1, kStepPrologueSwiGLU = 2 };
+enum StepEpilogue { kStepEpilogueNone = 0, kStepEpilogueSwiGLU = 1 };
+struct StepOp {
+  int kind, prologue, epilogue, n, k;  // GEMV / EMBED: weight rows n, columns k
+  int64_t S;                           // packed row stride
+  const uint8_t* W;
+  const float* x;         // GEMV input; ATTENTION: the qkv projection
+  float* y;               // GEMV / EMBED / ATTENTION output
+  const float* residual;  // GEMV: y = residual + W x
+  const float* norm_w;    // GEMV rms_norm prologue weight
+  float eps;
+  int argmax;             // GEMV: per-CTA row maxima for the ARGMAX operation
+  int rpc;                // GEMV rows per ring chunk
+  int hq, hkv, max_t;     // ATTENTION
+  float scale;
+  float* kc;
+  float* vc;
+  const float* cos_t;
+  const float* sin_t;
+  float* attn_part;       // ATTENTION: [hq][splits][132] partials (workspace)
+  unsigned* head_cnt;     // ATTENTION: [hq] arrival counters (zero between launches)
+};
+size_t step_smem_bytes();
+int step_rows_per_chunk(int64_t k);  // 0 if a row does not fit a ring slot
+int step_splits();
+cudaError_t step_max_grid(int device, int* grid);
+cudaError_t launch_decode_step(const StepOp* ops, int nops, int* pos, int* token, unsigned* done, float* am_gv,
+                               int* am_gi, int grid, int device, cudaStream_t s);
+cudaError_t read_step_fault(unsigned int* flags, bool clear);  // bit 4
 size_t argmax_workspace_bytes();
 cudaError_t launch_argmax(const float* logits, int n, void* ws, int* token, int* pos, cudaStream_t s);
 

@@ -179,14 +179,13 @@ class Q8Decoder:
         self.qkv, self.q = f(cfg.qkv_rows), f(cfg.heads * cfg.head_dim)
         self.attn, self.o_out, self.d_out = f(cfg.heads * cfg.head_dim), f(H), f(H)
         self.gu, self.logits = f(2 * cfg.inter), f(cfg.vocab)
+        self.hmid = f(cfg.inter)  # silu(gate) * up of the persistent step
         self.token = torch.zeros(1, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         L = _lib.lib()
         self.attn_ws = torch.zeros(L.q8lin_attention_workspace_size(cfg.heads, cfg.max_t), dtype=torch.uint8,
                                    device=dev)
         self.argmax_ws = torch.zeros(L.q8lin_argmax_workspace_size(), dtype=torch.uint8, device=dev)
-        self.ra_ws = torch.zeros(L.q8lin_rope_attention_workspace_size(cfg.heads, cfg.max_t), dtype=torch.uint8,
-                                 device=dev)
 
     @staticmethod
     def _p(t: torch.Tensor) -> ctypes.c_void_p:
@@ -197,16 +196,65 @@ class Q8Decoder:
         self.pos.zero_()
         self.token.fill_(int(token))
 
-    def step(self, fused: bool = True) -> None:
+    MODES = ("persistent", "fused", "unfused")
+
+    def step(self, mode: str = "persistent") -> None:
         """One decode step for the token at self.token / position self.pos; afterwards
         self.token holds the greedy next token, self.logits its logits, pos advanced.
-        fused: rms_norm and SwiGLU run inside the following projection's activation
-        quantization, the residual adds inside the o / down projections and RoPE + KV
-        append inside the attention kernel (5 launches per layer instead of 11)."""
-        if fused:
+
+        mode "persistent": the whole step is one cooperative launch of the persistent
+        decode-step kernel (q8lin_step_run), weights streamed ahead of the data;
+        "fused": one launch per operation with rms_norm and SwiGLU inside the following
+        projection's activation quantization, the residual adds inside the o / down
+        projections and RoPE + KV append inside the attention kernel (5 launches per
+        layer); "unfused": 11 launches per layer, one per reference operation."""
+        if mode == "persistent":
+            check(_lib.lib().q8lin_step_run(self._persistent(), ctypes.c_void_p(_stream_ptr(self.device))))
+        elif mode == "fused":
             self._step_fused()
-        else:
+        elif mode == "unfused":
             self._step_unfused()
+        else:
+            raise ValueError(f"mode must be one of {self.MODES}")
+
+    def _persistent(self) -> ctypes.c_void_p:
+        """The decode step as a q8lin_step program (built once, then reused)."""
+        if getattr(self, "_step_handle", None) is not None:
+            return self._step_handle
+        cfg, L, P = self.cfg, _lib.lib(), lambda t: t.data_ptr()
+        ops = [_lib.Op(kind=_lib.OP_EMBED, weight=self.embed.handle.value, y=P(self.x))]
+        for li, w in enumerate(self.layers):
+            ops.append(_lib.Op(kind=_lib.OP_GEMV, prologue=_lib.PROLOGUE_RMSNORM, weight=w["qkv"].handle.value,
+                               x=P(self.x), y=P(self.qkv), norm_weight=P(w["attn_norm"]), eps=cfg.eps))
+            ops.append(_lib.Op(kind=_lib.OP_ATTENTION, x=P(self.qkv), y=P(self.attn), k_cache=P(self.k_cache[li]),
+                               v_cache=P(self.v_cache[li]), cos_t=P(self.cos), sin_t=P(self.sin), hq=cfg.heads,
+                               hkv=cfg.kv_heads, head_dim=cfg.head_dim, max_t=cfg.max_t))
+            ops.append(_lib.Op(kind=_lib.OP_GEMV, weight=w["o"].handle.value, x=P(self.attn), y=P(self.x),
+                               residual=P(self.x)))
+            ops.append(_lib.Op(kind=_lib.OP_GEMV, prologue=_lib.PROLOGUE_RMSNORM, epilogue=_lib.EPILOGUE_SWIGLU,
+                               weight=w["gate_up"].handle.value, x=P(self.x), y=P(self.hmid),
+                               norm_weight=P(w["ffn_norm"]), eps=cfg.eps))
+            ops.append(_lib.Op(kind=_lib.OP_GEMV, weight=w["down"].handle.value, x=P(self.hmid), y=P(self.x),
+                               residual=P(self.x)))
+        ops.append(_lib.Op(kind=_lib.OP_GEMV, prologue=_lib.PROLOGUE_RMSNORM, weight=self.lm_head.handle.value,
+                           x=P(self.x), y=P(self.logits), norm_weight=P(self.out_norm), eps=cfg.eps, argmax=1))
+        ops.append(_lib.Op(kind=_lib.OP_ARGMAX))
+        arr = (_lib.Op * len(ops))(*ops)
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(L.q8lin_step_create(arr, len(ops), ctypes.c_void_p(P(self.pos)), ctypes.c_void_p(P(self.token)),
+                                      self.device.index, ctypes.byref(h)))
+        self._step_handle = h
+        return h
+
+    def __del__(self):
+        h = getattr(self, "_step_handle", None)
+        if h is not None and h.value:
+            try:
+                _lib.lib().q8lin_step_destroy(h)
+            except Exception:
+                pass
+            self._step_handle = None
 
     def _step_fused(self) -> None:
         cfg, L, P = self.cfg, _lib.lib(), self._p
@@ -216,8 +264,7 @@ class Q8Decoder:
             w["qkv"].forward_fused(self.x, self.qkv, QMatMul.PROLOGUE_RMSNORM, w["attn_norm"], cfg.eps)
             check(L.q8lin_rope_attention_decode(P(self.qkv), P(self.pos), P(self.cos), P(self.sin),
                                                 P(self.k_cache[li]), P(self.v_cache[li]), cfg.heads, cfg.kv_heads,
-                                                cfg.head_dim, cfg.max_t, P(self.ra_ws), self.ra_ws.numel(),
-                                                P(self.attn), s))
+                                                cfg.head_dim, cfg.max_t, P(self.attn), s))
             w["o"].forward_fused(self.attn, self.x, residual=self.x)
             w["gate_up"].forward_fused(self.x, self.gu, QMatMul.PROLOGUE_RMSNORM, w["ffn_norm"], cfg.eps)
             w["down"].forward_fused(self.gu, self.x, QMatMul.PROLOGUE_SWIGLU, residual=self.x)
@@ -250,7 +297,10 @@ class Q8Decoder:
         check(L.q8lin_argmax(P(self.logits), cfg.vocab, P(self.argmax_ws), self.argmax_ws.numel(), P(self.token),
                              P(self.pos), s))
 
-    def launches_per_step(self, fused: bool = True) -> int:
+    def launches_per_step(self, mode: str = "persistent") -> int:
+        if mode == "persistent":
+            return 1
+        fused = mode == "fused"
         return 1 + self.cfg.layers * (5 if fused else 11) + (2 if fused else 3)
 
     def weight_bytes_per_step(self) -> int:
