@@ -136,4 +136,64 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// ---------------------------------------------------------------------------
+// M = 1 row dot products over one 2048-value segment of a repacked row ([int8 K |
+// f16 d[K/32]]): lane l holds blocks b0 = 64 seg + l and b1 = b0 + 32 of the segment
+// (32 int8 each, two 16-byte units); per block the term is ((f32(isum) * dw) * dx) with
+// each product rounded (candle's scalar vec_dot), and the row sum is a tree over the
+// lanes.  Two rows at a time share the activation registers.
+struct XSeg {
+  int4 a0, a1, b0, b1;  // quantized activations of blocks b0 and b1
+  float da, db;         // their scales
+  bool va, vb;          // blocks inside K
+};
+
+// The warp's activation segment from the quantized vector in shared memory (qx int8
+// [K], dx f32 [K/32]; nb = K/32 blocks).
+__device__ __forceinline__ XSeg load_xseg(const int8_t* qx, const float* dx, int nb, int seg) {
+  const int lane = threadIdx.x & 31, b0 = seg * 64 + lane, b1 = b0 + 32;
+  XSeg xs;
+  xs.va = b0 < nb;
+  xs.vb = b1 < nb;
+  const int4 z = make_int4(0, 0, 0, 0);
+  xs.a0 = xs.va ? *reinterpret_cast<const int4*>(qx + (size_t)b0 * 32) : z;
+  xs.a1 = xs.va ? *reinterpret_cast<const int4*>(qx + (size_t)b0 * 32 + 16) : z;
+  xs.b0 = xs.vb ? *reinterpret_cast<const int4*>(qx + (size_t)b1 * 32) : z;
+  xs.b1 = xs.vb ? *reinterpret_cast<const int4*>(qx + (size_t)b1 * 32 + 16) : z;
+  xs.da = xs.va ? dx[b0] : 0.0f;
+  xs.db = xs.vb ? dx[b1] : 0.0f;
+  return xs;
+}
+
+__device__ __forceinline__ float block_term(const uint8_t* row, int K, int blk, const int4& x0, const int4& x1,
+                                            float dxs) {
+  const int4 w0 = *reinterpret_cast<const int4*>(row + (size_t)blk * 32);
+  const int4 w1 = *reinterpret_cast<const int4*>(row + (size_t)blk * 32 + 16);
+  const int isum = dot16(w1, x1, dot16(w0, x0, 0));
+  const float dw = __half2float(reinterpret_cast<const __half*>(row + K)[blk]);
+  return __fmul_rn(__fmul_rn(__int2float_rn(isum), dw), dxs);
+}
+
+__device__ __forceinline__ void seg_dot2(const uint8_t* wa, const uint8_t* wb, bool has_b, int K, int seg,
+                                         const XSeg& xs, float& sa, float& sb) {
+  const int lane = threadIdx.x & 31;
+  const int b0 = seg * 64 + lane, b1 = b0 + 32;
+  float ta = 0.0f, tb = 0.0f;
+  if (xs.va) {
+    ta = block_term(wa, K, b0, xs.a0, xs.a1, xs.da);
+    if (has_b) tb = block_term(wb, K, b0, xs.a0, xs.a1, xs.da);
+  }
+  if (xs.vb) {
+    ta = __fadd_rn(ta, block_term(wa, K, b1, xs.b0, xs.b1, xs.db));
+    if (has_b) tb = __fadd_rn(tb, block_term(wb, K, b1, xs.b0, xs.b1, xs.db));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ta += __shfl_xor_sync(kFull, ta, o);
+    tb += __shfl_xor_sync(kFull, tb, o);
+  }
+  sa = ta;
+  sb = tb;
+}
+
 }  // namespace q8lin

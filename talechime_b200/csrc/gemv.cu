@@ -195,6 +195,7 @@ constexpr int kSegUnits = 32 * kUnitsPerLane;  // 16-byte units per row segment 
 constexpr int kMaxSegs = 4;
 constexpr int kStreamMaxK = kMaxSegs * kSegUnits * 16;
 constexpr uint32_t kWaitLimit = 1u << 24;
+constexpr int kStreamResRows = 512;  // residual rows staged in shared memory
 
 __device__ unsigned int g_gemv_fault;
 
@@ -234,6 +235,7 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
   int* cnt = reinterpret_cast<int*>(part + kMaxSlots * kMaxRpc * kMaxSegs);
   uint64_t* full = reinterpret_cast<uint64_t*>(cnt + kMaxSlots * kMaxRpc);
   uint64_t* empty = full + kMaxSlots;
+  float* res_s = reinterpret_cast<float*>(empty + kMaxSlots);  // [kStreamResRows] residual rows of the CTA
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -290,6 +292,8 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
       }
     }
     pdl_wait();
+    if (fz.residual && r1 - r0 <= kStreamResRows && (int)threadIdx.x < r1 - r0)
+      res_s[threadIdx.x] = fz.residual[r0 + threadIdx.x];  // read before any row of this CTA is written
     if (fz.prologue == kPrologueSwiGLU) {
       // x = [gate | up], K values each: the activation is silu(gate) * up
 #pragma unroll
@@ -355,58 +359,49 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
 
   const int seg = warp % nseg, grp = warp / nseg;
   if (grp >= ngroups) return;  // K = 6144: one warp of the sixteen has no segment
-  int4 xr[kUnitsPerLane];
-  float dxr[kUnitsPerLane];
-#pragma unroll
-  for (int t = 0; t < kUnitsPerLane; ++t) {
-    const int u = seg * kSegUnits + 32 * t + lane;
-    xr[t] = u < nunits ? *reinterpret_cast<const int4*>(qx + (size_t)u * 16) : make_int4(0, 0, 0, 0);
-    dxr[t] = u < nunits ? dx[u >> 1] : 0.0f;
-  }
-
-  for (int rr = grp; rr < r1 - r0; rr += ngroups) {
-    const int j = rr / rpc, ri = rr % rpc;
-    const int slot = j % slots;
-    if (!bar_wait(&full[slot], (uint32_t)((j / slots) & 1))) break;
-    const uint8_t* wrow = ring + (size_t)slot * chunk_bytes + (size_t)ri * S;
-    const __half* wsc = reinterpret_cast<const __half*>(wrow + K);
-    int4 wv[kUnitsPerLane];
-#pragma unroll
-    for (int t = 0; t < kUnitsPerLane; ++t) {
-      const int u = seg * kSegUnits + 32 * t + lane;
-      wv[t] = u < nunits ? *reinterpret_cast<const int4*>(wrow + (size_t)u * 16) : make_int4(0, 0, 0, 0);
+  const XSeg xs = load_xseg(qx, dx, nb, seg);
+  const int nrows = r1 - r0;
+  const bool res_from_smem = nrows <= kStreamResRows;
+  // finalize row segment `rr` (chunk slot `slot`, row `ri` in the chunk) and release it
+  auto finish = [&](int rr, int slot, int ri, float v) {
+    if (nseg == 1) {
+      y[r0 + rr] = fz.residual ? __fadd_rn(res_from_smem ? res_s[rr] : fz.residual[r0 + rr], v) : v;
+    } else {
+      float* pr = part + (slot * kMaxRpc + ri) * kMaxSegs;
+      pr[seg] = v;
+      __threadfence_block();
+      if (atomicAdd(&cnt[slot * kMaxRpc + ri], 1) == nseg - 1) {
+        __threadfence_block();
+        float sum = pr[0];
+        for (int q = 1; q < nseg; ++q) sum += pr[q];
+        y[r0 + rr] = fz.residual ? __fadd_rn(res_from_smem ? res_s[rr] : fz.residual[r0 + rr], sum) : sum;
+        cnt[slot * kMaxRpc + ri] = 0;
+      }
     }
-    int is[kUnitsPerLane];
-#pragma unroll
-    for (int t = 0; t < kUnitsPerLane; ++t) is[t] = dot16(wv[t], xr[t], 0);
-#pragma unroll
-    for (int t = 0; t < kUnitsPerLane; ++t) is[t] += __shfl_xor_sync(kFull, is[t], 1);
-    float acc[kUnitsPerLane];
-#pragma unroll
-    for (int t = 0; t < kUnitsPerLane; ++t) {
-      const int u = seg * kSegUnits + 32 * t + lane;
-      acc[t] = 0.0f;
-      if (u < nunits && !(lane & 1))  // pairs (2p, 2p + 1) are valid together: nunits is even
-        acc[t] = __fmul_rn(__fmul_rn(__int2float_rn(is[t]), __half2float(wsc[u >> 1])), dxr[t]);
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[slot])) : "memory");
+  };
+  // two rows in flight per warp: rr and rr + ngroups (the ring holds every chunk the
+  // rows in flight of all warps can touch; checked by stream_plan's caller)
+  for (int rr = grp; rr < nrows; rr += 2 * ngroups) {
+    const int rb = rr + ngroups;
+    const bool has_b = rb < nrows;
+    const int ja = rr / rpc, ria = rr - ja * rpc, sa = ja % slots;
+    if (!bar_wait(&full[sa], (uint32_t)((ja / slots) & 1))) break;
+    int jb = ja, rib = ria, sb = sa;
+    if (has_b) {
+      jb = rb / rpc;
+      rib = rb - jb * rpc;
+      sb = jb % slots;
+      if (!bar_wait(&full[sb], (uint32_t)((jb / slots) & 1))) break;
     }
-    const float accs = warp_sum((acc[0] + acc[1]) + (acc[2] + acc[3]));
+    const uint8_t* wa = ring + (size_t)sa * chunk_bytes + (size_t)ria * S;
+    const uint8_t* wb = ring + (size_t)sb * chunk_bytes + (size_t)rib * S;
+    float va, vb;
+    seg_dot2(wa, wb, has_b, K, seg, xs, va, vb);
     __syncwarp();
     if (lane == 0) {
-      if (nseg == 1) {
-        y[r0 + rr] = fz.residual ? __fadd_rn(fz.residual[r0 + rr], accs) : accs;
-      } else {
-        float* pr = part + (slot * kMaxRpc + ri) * kMaxSegs;
-        pr[seg] = accs;
-        __threadfence_block();
-        if (atomicAdd(&cnt[slot * kMaxRpc + ri], 1) == nseg - 1) {
-          __threadfence_block();
-          float sum = pr[0];
-          for (int q = 1; q < nseg; ++q) sum += pr[q];
-          y[r0 + rr] = fz.residual ? __fadd_rn(fz.residual[r0 + rr], sum) : sum;
-          cnt[slot * kMaxRpc + ri] = 0;
-        }
-      }
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[slot])) : "memory");
+      finish(rr, sa, ria, va);
+      if (has_b) finish(rb, sb, rib, vb);
     }
   }
 }
@@ -424,7 +419,7 @@ void stream_plan(int64_t k, int64_t S, int* rpc, int* slots) {
 
 size_t stream_smem_bytes(int64_t k) {
   return (size_t)(kRingBytes + round16(k) + round16(4 * (k / kQK)) + kMaxSlots * kMaxRpc * kMaxSegs * 4 +
-                  kMaxSlots * kMaxRpc * 4 + 2 * kMaxSlots * 8);
+                  kMaxSlots * kMaxRpc * 4 + 2 * kMaxSlots * 8 + kStreamResRows * 4);
 }
 
 cudaError_t launch_stream(const q8lin_weight& w, const float* x, float* y, int rpc, int slots, cudaStream_t s,

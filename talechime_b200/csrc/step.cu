@@ -209,47 +209,6 @@ __device__ void gemv_prologue(const StepOp& op, const float4 (&wn)[kQuadGroups],
   }
 }
 
-// Segment dot products of two rows against the warp's activation segment.  Lane l
-// holds blocks b0 = 64 seg + l and b1 = b0 + 32 of the segment (32 int8 each, two
-// 16-byte units); per block the term is ((f32(isum) * dw) * dx) with each product
-// rounded, and the row sum is a tree over the lanes.
-struct XSeg {
-  int4 a0, a1, b0, b1;  // quantized activations of blocks b0 and b1
-  float da, db;         // their scales
-  bool va, vb;          // blocks inside K
-};
-
-__device__ __forceinline__ float block_term(const uint8_t* row, int K, int blk, const int4& x0, const int4& x1,
-                                            float dxs) {
-  const int4 w0 = *reinterpret_cast<const int4*>(row + (size_t)blk * 32);
-  const int4 w1 = *reinterpret_cast<const int4*>(row + (size_t)blk * 32 + 16);
-  const int isum = dot16(w1, x1, dot16(w0, x0, 0));
-  const float dw = __half2float(reinterpret_cast<const __half*>(row + K)[blk]);
-  return __fmul_rn(__fmul_rn(__int2float_rn(isum), dw), dxs);
-}
-
-__device__ __forceinline__ void seg_dot2(const uint8_t* wa, const uint8_t* wb, bool has_b, int K, int seg,
-                                         const XSeg& xs, float& sa, float& sb) {
-  const int lane = threadIdx.x & 31;
-  const int b0 = seg * 64 + lane, b1 = b0 + 32;
-  float ta = 0.0f, tb = 0.0f;
-  if (xs.va) {
-    ta = block_term(wa, K, b0, xs.a0, xs.a1, xs.da);
-    if (has_b) tb = block_term(wb, K, b0, xs.a0, xs.a1, xs.da);
-  }
-  if (xs.vb) {
-    ta = __fadd_rn(ta, block_term(wa, K, b1, xs.b0, xs.b1, xs.db));
-    if (has_b) tb = __fadd_rn(tb, block_term(wb, K, b1, xs.b0, xs.b1, xs.db));
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    ta += __shfl_xor_sync(kFull, ta, o);
-    tb += __shfl_xor_sync(kFull, tb, o);
-  }
-  sa = ta;
-  sb = tb;
-}
-
 // One GEMV operation on the consumer side.  `seq` is the ring position of its first
 // chunk.  A warp touches only the chunks in which it has pairs; each such warp adds its
 // pair count to the chunk's shared-memory tally and the warp that completes the tally
@@ -274,21 +233,8 @@ __device__ void gemv_consume(const StepOp& op, int c, int g, int seq, uint8_t* s
   const bool res_smem = op.residual && nunits_cta <= kSMaxResidualRows;
   const float* residual = op.residual;
   float* y = op.y;
-  XSeg xs;
-  {
-    const int8_t* qx = reinterpret_cast<const int8_t*>(sm + SmemLayout::qx);
-    const float* dx = reinterpret_cast<const float*>(sm + SmemLayout::dx);
-    const int b0 = seg * 64 + lane, b1 = b0 + 32;
-    xs.va = b0 < nb;
-    xs.vb = b1 < nb;
-    const int4 z = make_int4(0, 0, 0, 0);
-    xs.a0 = xs.va ? *reinterpret_cast<const int4*>(qx + (size_t)b0 * 32) : z;
-    xs.a1 = xs.va ? *reinterpret_cast<const int4*>(qx + (size_t)b0 * 32 + 16) : z;
-    xs.b0 = xs.vb ? *reinterpret_cast<const int4*>(qx + (size_t)b1 * 32) : z;
-    xs.b1 = xs.vb ? *reinterpret_cast<const int4*>(qx + (size_t)b1 * 32 + 16) : z;
-    xs.da = xs.va ? dx[b0] : 0.0f;
-    xs.db = xs.vb ? dx[b1] : 0.0f;
-  }
+  const XSeg xs = load_xseg(reinterpret_cast<const int8_t*>(sm + SmemLayout::qx),
+                            reinterpret_cast<const float*>(sm + SmemLayout::dx), nb, seg);
   float bv = -INFINITY;
   int bi = op.n;
   // finalize one row value (row index `r` within the CTA's rows)
