@@ -143,33 +143,42 @@ __device__ __forceinline__ float warp_sum(float v) {
 // each product rounded (candle's scalar vec_dot), and the row sum is a tree over the
 // lanes.  Two rows at a time share the activation registers.
 struct XSeg {
-  int4 a0, a1, b0, b1;  // quantized activations of blocks b0 and b1
+  int4 a0, a1, b0, b1;  // quantized activations of blocks b0 and b1, halves in load order
   float da, db;         // their scales
   bool va, vb;          // blocks inside K
 };
+
+// A lane reads the two 16-byte halves of its 32-byte block in the order (lane ^ lane/4)
+// & 1 first: within each group of 8 lanes (one shared-memory wavefront of 16-byte
+// accesses) the 8 accesses then fall on 8 distinct 4-bank groups, where reading the
+// low half first in every lane would put lanes l and l + 4 on the same banks.
+__device__ __forceinline__ int half_order(int lane) { return (lane ^ (lane >> 2)) & 1; }
 
 // The warp's activation segment from the quantized vector in shared memory (qx int8
 // [K], dx f32 [K/32]; nb = K/32 blocks).
 __device__ __forceinline__ XSeg load_xseg(const int8_t* qx, const float* dx, int nb, int seg) {
   const int lane = threadIdx.x & 31, b0 = seg * 64 + lane, b1 = b0 + 32;
+  const int h = half_order(lane) * 16;
   XSeg xs;
   xs.va = b0 < nb;
   xs.vb = b1 < nb;
   const int4 z = make_int4(0, 0, 0, 0);
-  xs.a0 = xs.va ? *reinterpret_cast<const int4*>(qx + (size_t)b0 * 32) : z;
-  xs.a1 = xs.va ? *reinterpret_cast<const int4*>(qx + (size_t)b0 * 32 + 16) : z;
-  xs.b0 = xs.vb ? *reinterpret_cast<const int4*>(qx + (size_t)b1 * 32) : z;
-  xs.b1 = xs.vb ? *reinterpret_cast<const int4*>(qx + (size_t)b1 * 32 + 16) : z;
+  xs.a0 = xs.va ? *reinterpret_cast<const int4*>(qx + (size_t)b0 * 32 + h) : z;
+  xs.a1 = xs.va ? *reinterpret_cast<const int4*>(qx + (size_t)b0 * 32 + (16 - h)) : z;
+  xs.b0 = xs.vb ? *reinterpret_cast<const int4*>(qx + (size_t)b1 * 32 + h) : z;
+  xs.b1 = xs.vb ? *reinterpret_cast<const int4*>(qx + (size_t)b1 * 32 + (16 - h)) : z;
   xs.da = xs.va ? dx[b0] : 0.0f;
   xs.db = xs.vb ? dx[b1] : 0.0f;
   return xs;
 }
 
+// Block `blk` of a row against activations x0 / x1 held in the same half order.
 __device__ __forceinline__ float block_term(const uint8_t* row, int K, int blk, const int4& x0, const int4& x1,
                                             float dxs) {
-  const int4 w0 = *reinterpret_cast<const int4*>(row + (size_t)blk * 32);
-  const int4 w1 = *reinterpret_cast<const int4*>(row + (size_t)blk * 32 + 16);
-  const int isum = dot16(w1, x1, dot16(w0, x0, 0));
+  const int h = half_order(threadIdx.x & 31) * 16;
+  const int4 w0 = *reinterpret_cast<const int4*>(row + (size_t)blk * 32 + h);
+  const int4 w1 = *reinterpret_cast<const int4*>(row + (size_t)blk * 32 + (16 - h));
+  const int isum = dot16(w1, x1, dot16(w0, x0, 0));  // exact in int32 either way
   const float dw = __half2float(reinterpret_cast<const __half*>(row + K)[blk]);
   return __fmul_rn(__fmul_rn(__int2float_rn(isum), dw), dxs);
 }

@@ -380,28 +380,39 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
     }
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[slot])) : "memory");
   };
+  // Ring position of a row, advanced incrementally (no division in the loop).
+  struct Pos {
+    int ri, slot;
+    uint32_t parity;
+  };
+  auto advance = [&](Pos p, int rows) {
+    p.ri += rows;
+    while (p.ri >= rpc) {
+      p.ri -= rpc;
+      if (++p.slot == slots) {
+        p.slot = 0;
+        p.parity ^= 1u;
+      }
+    }
+    return p;
+  };
   // two rows in flight per warp: rr and rr + ngroups (the ring holds every chunk the
   // rows in flight of all warps can touch; checked by stream_plan's caller)
-  for (int rr = grp; rr < nrows; rr += 2 * ngroups) {
+  Pos pa = advance(Pos{0, 0, 0u}, grp);
+  for (int rr = grp; rr < nrows; rr += 2 * ngroups, pa = advance(pa, 2 * ngroups)) {
     const int rb = rr + ngroups;
     const bool has_b = rb < nrows;
-    const int ja = rr / rpc, ria = rr - ja * rpc, sa = ja % slots;
-    if (!bar_wait(&full[sa], (uint32_t)((ja / slots) & 1))) break;
-    int jb = ja, rib = ria, sb = sa;
-    if (has_b) {
-      jb = rb / rpc;
-      rib = rb - jb * rpc;
-      sb = jb % slots;
-      if (!bar_wait(&full[sb], (uint32_t)((jb / slots) & 1))) break;
-    }
-    const uint8_t* wa = ring + (size_t)sa * chunk_bytes + (size_t)ria * S;
-    const uint8_t* wb = ring + (size_t)sb * chunk_bytes + (size_t)rib * S;
+    if (!bar_wait(&full[pa.slot], pa.parity)) break;
+    const Pos pb = has_b ? advance(pa, ngroups) : pa;
+    if (has_b && !bar_wait(&full[pb.slot], pb.parity)) break;
+    const uint8_t* wa = ring + (size_t)pa.slot * chunk_bytes + (size_t)pa.ri * S;
+    const uint8_t* wb = ring + (size_t)pb.slot * chunk_bytes + (size_t)pb.ri * S;
     float va, vb;
     seg_dot2(wa, wb, has_b, K, seg, xs, va, vb);
     __syncwarp();
     if (lane == 0) {
-      finish(rr, sa, ria, va);
-      if (has_b) finish(rb, sb, rib, vb);
+      finish(rr, pa.slot, pa.ri, va);
+      if (has_b) finish(rb, pb.slot, pb.ri, vb);
     }
   }
 }

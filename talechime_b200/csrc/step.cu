@@ -315,7 +315,41 @@ __device__ void gemv_consume(const StepOp& op, int c, int g, int seq, uint8_t* s
 
 // RoPE + KV append + partial attention for unit (h, split); the last unit of head h
 // merges the head (all consumers).
-__device__ void attention_unit(const StepOp& op, int unit, int pos, uint8_t* sm) {
+// The first group of K and V rows of a warp (up to four cached positions), loaded before
+// the dependency wait: cached rows below pos were written by earlier launches.
+struct KVFirst {
+  float4 k[4], v[4];
+};
+
+__device__ __forceinline__ void attention_unit_range(int len, int split, int& a, int& b) {
+  const int per = (len + kSplits - 1) / kSplits;
+  a = min(len, split * per);
+  b = min(len, a + per);
+}
+
+__device__ void attention_prefetch(const StepOp* gop, int unit, int pos, KVFirst& f) {
+  constexpr int D = 128;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hq = __ldg(&gop->hq), hkv = __ldg(&gop->hkv), max_t = __ldg(&gop->max_t);
+  const int h = unit / kSplits, split = unit % kSplits, hk = h / (hq / hkv);
+  const int len = pos < 0 ? 0 : min(pos + 1, max_t);
+  int a, b;
+  attention_unit_range(len, split, a, b);
+  const float* kh = gop->kc + (size_t)hk * max_t * D;
+  const float* vh = gop->vc + (size_t)hk * max_t * D;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int t = a + warp + u * kSWarps;
+    if (t < b && t != pos) {
+      f.k[u] = ldcg4(kh + (size_t)t * D + 4 * lane);
+      f.v[u] = ldcg4(vh + (size_t)t * D + 4 * lane);
+    } else {
+      f.k[u] = f.v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+}
+
+__device__ void attention_unit(const StepOp& op, int unit, int pos, uint8_t* sm, const KVFirst* first) {
   constexpr int D = 128, half = 64;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = unit / kSplits, split = unit % kSplits;
@@ -326,8 +360,8 @@ __device__ void attention_unit(const StepOp& op, int unit, int pos, uint8_t* sm)
   float* awp = reinterpret_cast<float*>(sm + SmemLayout::awp);
   int* flag = reinterpret_cast<int*>(sm + SmemLayout::flag);
   const int len = pos < 0 ? 0 : min(pos + 1, max_t);
-  const int per = (len + kSplits - 1) / kSplits;
-  const int a = min(len, split * per), b = min(len, a + per);
+  int a, b;
+  attention_unit_range(len, split, a, b);
   const bool cur = a <= pos && pos < b;
   if (tid < D && pos >= 0 && pos < max_t) {
     const int j = tid < half ? tid : tid - half;
@@ -357,17 +391,21 @@ __device__ void attention_unit(const StepOp& op, int unit, int pos, uint8_t* sm)
   // warp w: positions a + w, a + w + 16, ...; four positions' K and V rows in flight
   for (int t0 = a + warp; t0 < b; t0 += 4 * kSWarps) {
     float4 k4[4], v4[4];
+    const bool pre = first && t0 == a + warp;
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int t = t0 + u * kSWarps;
       if (t >= b) {
         k4[u] = v4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      } else if (t != pos) {
-        k4[u] = ldcg4(kh + (size_t)t * D + 4 * lane);
-        v4[u] = ldcg4(vh + (size_t)t * D + 4 * lane);
-      } else {  // the current token: rotated in this launch, not read back from the cache
+      } else if (t == pos) {  // the current token: rotated in this launch, not read back from the cache
         k4[u] = reinterpret_cast<const float4*>(akc)[lane];
         v4[u] = reinterpret_cast<const float4*>(avc)[lane];
+      } else if (pre) {
+        k4[u] = first->k[u];
+        v4[u] = first->v[u];
+      } else {
+        k4[u] = ldcg4(kh + (size_t)t * D + 4 * lane);
+        v4[u] = ldcg4(vh + (size_t)t * D + 4 * lane);
       }
     }
     float s[4];
@@ -518,13 +556,15 @@ decode_step_kernel(const StepOp* __restrict__ ops, int nops, int* __restrict__ p
   // The operation descriptor is copied to shared memory before the dependency wait: the
   // acquire of the wait discards L1, and the descriptor is read again after every
   // barrier wait of the ring, so global reads of it would cost L2 round trips.
-  __shared__ int s_pos;
   __shared__ __align__(16) StepOp s_op[2];  // double-buffered: op o + 1 is written while slow threads may still read op o
   constexpr int kOpWords = (int)(sizeof(StepOp) / 4);
   static_assert(sizeof(StepOp) % 4 == 0 && kOpWords <= kSConsumers, "descriptor copy");
   float* am_v = reinterpret_cast<float*>(sm + SmemLayout::amv);
   int* am_i = reinterpret_cast<int*>(sm + SmemLayout::ami);
   float* res = reinterpret_cast<float*>(sm + SmemLayout::res);
+  // the position of this step: written only by the ARGMAX operation at the end of the
+  // launch, so one read serves every operation
+  const int pos = __ldcg(pos_dev);
   int seq = 0;
   for (int o = 0; o < nops; ++o) {
     if (tid < kOpWords)
@@ -543,11 +583,11 @@ decode_step_kernel(const StepOp* __restrict__ ops, int nops, int* __restrict__ p
         }
       }
     }
+    KVFirst kvf;
+    const bool attn_first = __ldg(&ops[o].kind) == kStepOpAttention && c < __ldg(&ops[o].hq) * kSplits;
+    if (attn_first) attention_prefetch(ops + o, c, pos, kvf);
     const StepOp& op = s_op[o & 1];
-    if (tid == 0) {
-      if (o > 0) wait_count(done + o - 1, (unsigned)g);
-      if (op.kind == kStepOpAttention || op.kind == kStepOpArgmax) s_pos = __ldcg(pos_dev);
-    }
+    if (tid == 0 && o > 0) wait_count(done + o - 1, (unsigned)g);
     consumers_sync();
     if (op.kind == kStepOpGemv) {
       int u0, u1;
@@ -574,9 +614,8 @@ decode_step_kernel(const StepOp* __restrict__ ops, int nops, int* __restrict__ p
         am_gi[c] = bi;
       }
     } else if (op.kind == kStepOpAttention) {
-      const int pos = s_pos;
       for (int unit = c; unit < op.hq * kSplits; unit += g) {
-        attention_unit(op, unit, pos, sm);
+        attention_unit(op, unit, pos, sm, unit == c && attn_first ? &kvf : nullptr);
         consumers_sync();
       }
     } else if (op.kind == kStepOpEmbed) {
@@ -591,7 +630,6 @@ decode_step_kernel(const StepOp* __restrict__ ops, int nops, int* __restrict__ p
       consumers_sync();
     } else if (op.kind == kStepOpArgmax && c == 0) {
       // lowest index among equal maxima; NaN compares as smaller
-      const int pos = s_pos;
       float bv = -INFINITY;
       int bi = op.n;
       for (int i = tid; i < g; i += kSConsumers) {
