@@ -332,7 +332,9 @@ def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, step
     RMSNorm, RoPE, f32 KV cache, vocab 73448; talechime_b200/decoder.py), batch 1: a
     128-token random-id prefix, then `steps` greedy decode steps replayed from one CUDA
     graph of a step; device time of the decode steps (CUDA events), max over ranks (one
-    independent replica per GPU)."""
+    independent replica per GPU).  Both step implementations are timed: "fused" (one
+    launch per operation, the default) and "persistent" (one cooperative launch per
+    step)."""
     from talechime_b200.decoder import DecoderConfig, Q8Decoder, synthetic_weights
 
     cfg = DecoderConfig(max_t=prefix + steps)
@@ -344,43 +346,51 @@ def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, step
     gen = torch.Generator()
     gen.manual_seed(99)
     ids = torch.randint(0, cfg.vocab, (prefix,), generator=gen).tolist()
-    with torch.cuda.stream(stream):
-        dec.reset(ids[0])
-        dec.step()  # eager warm-up: workspaces and kernel attributes outside the capture
-        dec.reset(ids[0])
-        torch.cuda.synchronize(dev)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            dec.step()
-        dec.reset(ids[0])
-        for t in ids:  # prefix, one position per replay (the argmax output is overwritten)
-            dec.token.fill_(t)
-            graph.replay()
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(steps):
-            graph.replay()
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
     wbytes = dec.weight_bytes_per_step()
     # KV cache read per step at position p: layers * 2 * kv_heads * (p + 1) * head_dim * 4
     kv_bytes = sum(cfg.layers * 2 * cfg.kv_heads * (p + 1) * cfg.head_dim * 4 for p in range(prefix, prefix + steps))
+    results = {}
+    for mode in ("fused", "persistent"):
+        with torch.cuda.stream(stream):
+            dec.reset(ids[0])
+            dec.step(mode)  # eager warm-up: workspaces and kernel attributes outside the capture
+            dec.reset(ids[0])
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                dec.step(mode)
+            dec.reset(ids[0])
+            for t in ids:  # prefix, one position per replay (the argmax output is overwritten)
+                dec.token.fill_(t)
+                graph.replay()
+            torch.cuda.synchronize(dev)
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        results[mode] = (ms, int(dec.pos.item()))
+        del graph
+    ms, final_pos = results["fused"]
+    msp, _ = results["persistent"]
     out = {"config": "Q8_0 decoder, hidden 2048, 28 layers, 16 x 128 heads (MHA), SwiGLU 6144, RMSNorm, RoPE, "
                      f"f32 KV cache, vocab 73448; batch 1, {prefix}-token random-id prefix, {steps} greedy steps",
            "tokens_per_s": world * steps / (ms * 1e-3), "ms_per_token": ms / steps,
+           "tokens_per_s_persistent": world * steps / (msp * 1e-3), "ms_per_token_persistent": msp / steps,
            "weight_bytes_per_token": wbytes, "kv_bytes_per_token_avg": kv_bytes / steps,
            "hbm_tb_s": (wbytes * steps + kv_bytes) / (ms * 1e-3) / 1e12 * world,
-           "launches_per_token": dec.launches_per_step(), "final_position": int(dec.pos.item()),
-           "graph": "one CUDA graph of a decode step, replayed per token"}
-    del graph, dec
+           "launches_per_token": dec.launches_per_step("fused"), "launches_per_token_persistent": 1,
+           "final_position": final_pos,
+           "graph": "one CUDA graph of a decode step per mode, replayed per token"}
+    del dec
     torch.cuda.synchronize(dev)
     return out
 

@@ -198,7 +198,7 @@ class Q8Decoder:
 
     MODES = ("persistent", "fused", "unfused")
 
-    def step(self, mode: str = "persistent") -> None:
+    def step(self, mode: str = "fused") -> None:
         """One decode step for the token at self.token / position self.pos; afterwards
         self.token holds the greedy next token, self.logits its logits, pos advanced.
 
@@ -297,7 +297,7 @@ class Q8Decoder:
         check(L.q8lin_argmax(P(self.logits), cfg.vocab, P(self.argmax_ws), self.argmax_ws.numel(), P(self.token),
                              P(self.pos), s))
 
-    def launches_per_step(self, mode: str = "persistent") -> int:
+    def launches_per_step(self, mode: str = "fused") -> int:
         if mode == "persistent":
             return 1
         fused = mode == "fused"
