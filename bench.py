@@ -395,6 +395,42 @@ def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, step
     return out
 
 
+def run_profile_decoder(args) -> None:
+    """A short decoder run for ncu captures: 4 eager steps (warm-up launches to skip with
+    ncu -s), then 8 steps replayed from one CUDA graph, from position 380."""
+    import torch
+    from talechime_b200 import build
+    from talechime_b200.decoder import DecoderConfig, Q8Decoder, synthetic_weights
+
+    build.build()
+    dev = torch.device("cuda", 0)
+    cfg = DecoderConfig(layers=args.layers, max_t=640)
+    weights = synthetic_weights(cfg, seed=777, device=dev)
+    dec = Q8Decoder(cfg, weights, device=dev)
+    del weights
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        dec.reset(5)
+        dec.pos.fill_(380)
+        for _ in range(4):
+            dec.step(args.profile_decoder)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            dec.step(args.profile_decoder)
+        dec.pos.fill_(380)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(8):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    print(json.dumps({"profile_decoder": args.profile_decoder, "layers": cfg.layers,
+                      "launches_per_step": dec.launches_per_step(args.profile_decoder),
+                      "us_per_step": e0.elapsed_time(e1) * 1000 / 8}), flush=True)
+    del graph
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -412,6 +448,9 @@ def main() -> None:
                     help="M:K:N -- run one projection shape `--steps` times (profiling), print its timing")
     ap.add_argument("--sweep", action="store_true",
                     help="also time the BASELINE configs[1] shape sweep (M x {qkv,o,gate_up,down}) into the line")
+    ap.add_argument("--profile-decoder", default=None, choices=["fused", "persistent", "unfused"],
+                    help="profiling run: only the decoder, `--layers` layers, 8 steps replayed from a graph "
+                         "after 4 eager warm-up steps from position 380; prints its timing")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -428,6 +467,9 @@ def main() -> None:
 
     if args.case:
         run_case(args)
+        return
+    if args.profile_decoder:
+        run_profile_decoder(args)
         return
 
     torch.cuda.set_device(local_rank)
