@@ -322,6 +322,28 @@ def run_tp_mlp(torch, dist, dev, rank: int, world: int, reps: int = 20) -> dict:
             ms = float(t.item())
         out["per_m"].append({"m": m, "ms": ms, "weight_tb_s": weight_bytes / (ms * 1e-3) / 1e12,
                              "tokens_per_s": m / (ms * 1e-3), "tflops": 2.0 * 3 * inter * hidden * m / (ms * 1e-3) / 1e12})
+    if world > 1:
+        # decode rows with the down projection and the cross-GPU sum in one kernel
+        mlp.enable_fused_allreduce()
+        x = torch.randn((1, hidden), generator=gen, device=dev)
+        for _ in range(3):
+            mlp.forward(x)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            mlp.forward(x)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        out["m1_fused_allreduce"] = {"m": 1, "ms": ms, "weight_tb_s": weight_bytes / (ms * 1e-3) / 1e12,
+                                     "path": "gate_up GEMV, SwiGLU, down GEMV + cross-GPU sum in one kernel "
+                                             "(peer stores over NVLink, q8lin_forward_allreduce)"}
+        mlp.close_fused_allreduce()
     del mlp
     torch.cuda.synchronize(dev)
     return out

@@ -201,6 +201,32 @@ int q8lin_argmax(const float* logits, int64_t n, void* workspace, size_t workspa
                  q8lin_stream_t stream);
 
 /*
+ * Tensor-parallel down projection with the cross-GPU sum fused into the GEMV (M = 1,
+ * K <= 8192): y = [residual +] sum over the `world` ranks of W_rank . x_rank, each rank's
+ * rows pushed into every rank's staging buffer over NVLink (peer stores) and added in rank
+ * order (deterministic; bit-identical to a two-rank NCCL sum).  Replaces the partial
+ * down projection + all-reduce of the tensor-parallel MLP (crates/voxcpm/src/transformer.rs
+ * :147-150 split over GPUs).  Buffers: one staging buffer of
+ * q8lin_allreduce_stage_bytes(N, world) and one flag buffer of
+ * q8lin_allreduce_flag_bytes(world) per rank, allocated with q8lin_peer_alloc (zeroed; its
+ * IPC handle, Q8LIN_IPC_HANDLE_BYTES bytes, is exchanged out of band and opened on the other
+ * ranks with q8lin_peer_open).  stage_ptrs / flag_ptrs: DEVICE arrays of `world` pointers,
+ * entry r = rank r's buffer as mapped on this GPU.  epoch: the call count, 1, 2, ... (every
+ * rank passes the same value; all ranks must make every call).  A rank that never arrives
+ * makes the others time out (fault word bit 1) instead of hanging.
+ */
+#define Q8LIN_IPC_HANDLE_BYTES 64
+int q8lin_peer_alloc(int device, size_t bytes, void** ptr, void* ipc_handle);
+int q8lin_peer_open(int device, const void* ipc_handle, void** ptr);
+int q8lin_peer_close(int device, void* ptr);
+int q8lin_peer_free(int device, void* ptr);
+size_t q8lin_allreduce_stage_bytes(int64_t n, int32_t world);
+size_t q8lin_allreduce_flag_bytes(int32_t world);
+int q8lin_forward_allreduce(const q8lin_weight* w, const float* x, float* y, int64_t m, void* const* stage_ptrs,
+                            void* const* flag_ptrs, int32_t rank, int32_t world, uint32_t epoch,
+                            const float* residual, q8lin_stream_t stream);
+
+/*
  * Persistent decode step: a program of operations run by ONE cooperative launch (one
  * CTA per SM).  The weights of every GEMV stream through each SM's shared-memory ring
  * ahead of the data; operation i starts when every CTA has finished operation i - 1.

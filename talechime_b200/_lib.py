@@ -74,6 +74,14 @@ SIGNATURES = {
     "q8lin_rope_attention_decode": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_int32, ctypes.c_int32,
                                                    ctypes.c_int32, ctypes.c_int32, _c_p, _c_p]),
     "q8lin_add": (ctypes.c_int, [_c_p, _c_p, _i64, _c_p]),
+    "q8lin_peer_alloc": (ctypes.c_int, [ctypes.c_int, ctypes.c_size_t, ctypes.POINTER(_c_p), _c_p]),
+    "q8lin_peer_open": (ctypes.c_int, [ctypes.c_int, _c_p, ctypes.POINTER(_c_p)]),
+    "q8lin_peer_close": (ctypes.c_int, [ctypes.c_int, _c_p]),
+    "q8lin_peer_free": (ctypes.c_int, [ctypes.c_int, _c_p]),
+    "q8lin_allreduce_stage_bytes": (ctypes.c_size_t, [_i64, ctypes.c_int32]),
+    "q8lin_allreduce_flag_bytes": (ctypes.c_size_t, [ctypes.c_int32]),
+    "q8lin_forward_allreduce": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, ctypes.c_int32, ctypes.c_int32,
+                                               ctypes.c_uint32, _c_p, _c_p]),
     "q8lin_step_create": (ctypes.c_int, [ctypes.POINTER(Op), ctypes.c_int32, _c_p, _c_p, ctypes.c_int,
                                          ctypes.POINTER(_c_p)]),
     "q8lin_step_run": (ctypes.c_int, [_c_p, _c_p]),

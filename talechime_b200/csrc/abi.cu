@@ -1,6 +1,7 @@
 // C ABI of libq8lin.so (declared in include/q8lin.h): argument checks, weight
 // upload/repack, workspace management and dispatch to the kernels.
 #include <climits>
+#include <cstring>
 #include <cuda_runtime.h>
 #include <stdlib.h>
 
@@ -411,6 +412,94 @@ int q8lin_forward_fused(const q8lin_weight* w, const float* x, float* y, int64_t
   f.residual = residual;
   cudaError_t e = launch_gemv_fused(*w, x, y, f, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "fused gemv launch");
+  return Q8LIN_OK;
+}
+
+int q8lin_peer_alloc(int device, size_t bytes, void** ptr, void* ipc_handle) {
+  if (!ptr || !ipc_handle || bytes == 0) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "peer_alloc needs bytes > 0, ptr and handle");
+  *ptr = nullptr;
+  int st = check_device(device);
+  if (st != Q8LIN_OK) return st;
+  DeviceGuard guard(device);
+  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "peer buffer");
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return Q8LIN_OK;
+}
+
+int q8lin_peer_open(int device, const void* ipc_handle, void** ptr) {
+  if (!ptr || !ipc_handle) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "peer_open needs a handle and ptr");
+  *ptr = nullptr;
+  int st = check_device(device);
+  if (st != Q8LIN_OK) return st;
+  DeviceGuard guard(device);
+  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  return Q8LIN_OK;
+}
+
+int q8lin_peer_close(int device, void* ptr) {
+  if (!ptr) return Q8LIN_OK;
+  DeviceGuard guard(device);
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  return Q8LIN_OK;
+}
+
+int q8lin_peer_free(int device, void* ptr) {
+  if (!ptr) return Q8LIN_OK;
+  DeviceGuard guard(device);
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree(peer buffer)");
+  return Q8LIN_OK;
+}
+
+size_t q8lin_allreduce_stage_bytes(int64_t n, int32_t world) {
+  return (n > 0 && world > 0) ? (size_t)2 * (size_t)world * (size_t)n * sizeof(float) : 0;
+}
+
+size_t q8lin_allreduce_flag_bytes(int32_t world) {
+  return world > 0 ? (size_t)kAllreduceMaxCtas * (size_t)world * sizeof(uint32_t) : 0;
+}
+
+int q8lin_forward_allreduce(const q8lin_weight* w, const float* x, float* y, int64_t m, void* const* stage_ptrs,
+                            void* const* flag_ptrs, int32_t rank, int32_t world, uint32_t epoch,
+                            const float* residual, q8lin_stream_t stream) {
+  int st = validate_weight(w);
+  if (st != Q8LIN_OK) return st;
+  if (m != 1) return fail(Q8LIN_ERR_SHAPE, "the fused all-reduce takes one activation row (decode), got M=" + std::to_string(m));
+  if (w->k > kFusedMaxK) return fail(Q8LIN_ERR_SHAPE, "the fused all-reduce needs K <= 8192");
+  if (world < 1 || rank < 0 || rank >= world) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "rank must lie in [0, world)");
+  if (epoch == 0) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "epoch counts calls from 1");
+  if (!x || !y || (world > 1 && (!stage_ptrs || !flag_ptrs)))
+    return fail(Q8LIN_ERR_INVALID_ARGUMENT, "x, y and (world > 1) the peer pointer arrays must be non-null");
+  if (!aligned16(x) || !aligned16(y)) return fail(Q8LIN_ERR_ALIGNMENT, "x and y must be 16-byte aligned");
+  if (residual && (reinterpret_cast<uintptr_t>(residual) & 3u))
+    return fail(Q8LIN_ERR_ALIGNMENT, "residual must be 4-byte aligned");
+  if (sm_count(w->device) > kAllreduceMaxCtas) return fail(Q8LIN_ERR_DEVICE, "more SMs than the flag array covers");
+  DeviceGuard guard(w->device);
+  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
+  GemvFusion f;
+  f.residual = residual;
+  f.ar_stage = reinterpret_cast<float* const*>(stage_ptrs);
+  f.ar_flags = reinterpret_cast<unsigned* const*>(flag_ptrs);
+  f.ar_rank = rank;
+  f.ar_world = world;
+  f.ar_epoch = epoch;
+  cudaError_t e = launch_gemv_fused(*w, x, y, f, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fused gemv + all-reduce launch");
   return Q8LIN_OK;
 }
 

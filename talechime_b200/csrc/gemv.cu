@@ -196,6 +196,7 @@ constexpr int kMaxSegs = 4;
 constexpr int kStreamMaxK = kMaxSegs * kSegUnits * 16;
 constexpr uint32_t kWaitLimit = 1u << 24;
 constexpr int kStreamResRows = 512;  // residual rows staged in shared memory
+constexpr uint32_t kPeerWaitLimit = 1u << 20;  // polls of a peer's flag (~1 s with the back-off)
 
 __device__ unsigned int g_gemv_fault;
 
@@ -358,14 +359,22 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");  // consumer warps only
 
   const int seg = warp % nseg, grp = warp / nseg;
-  if (grp >= ngroups) return;  // K = 6144: one warp of the sixteen has no segment
-  const XSeg xs = load_xseg(qx, dx, nb, seg);
   const int nrows = r1 - r0;
   const bool res_from_smem = nrows <= kStreamResRows;
+  const bool allreduce = fz.ar_world > 1;
+  // the row's value: written to y, or (cross-GPU sum) staged on every rank
+  auto emit = [&](int rr, float v) {
+    if (allreduce) {
+      const size_t at = ((size_t)(fz.ar_epoch & 1u) * fz.ar_world + fz.ar_rank) * N + r0 + rr;
+      for (int p = 0; p < fz.ar_world; ++p) fz.ar_stage[p][at] = v;
+    } else {
+      y[r0 + rr] = fz.residual ? __fadd_rn(res_from_smem ? res_s[rr] : fz.residual[r0 + rr], v) : v;
+    }
+  };
   // finalize row segment `rr` (chunk slot `slot`, row `ri` in the chunk) and release it
   auto finish = [&](int rr, int slot, int ri, float v) {
     if (nseg == 1) {
-      y[r0 + rr] = fz.residual ? __fadd_rn(res_from_smem ? res_s[rr] : fz.residual[r0 + rr], v) : v;
+      emit(rr, v);
     } else {
       float* pr = part + (slot * kMaxRpc + ri) * kMaxSegs;
       pr[seg] = v;
@@ -374,7 +383,7 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
         __threadfence_block();
         float sum = pr[0];
         for (int q = 1; q < nseg; ++q) sum += pr[q];
-        y[r0 + rr] = fz.residual ? __fadd_rn(res_from_smem ? res_s[rr] : fz.residual[r0 + rr], sum) : sum;
+        emit(rr, sum);
         cnt[slot * kMaxRpc + ri] = 0;
       }
     }
@@ -398,8 +407,10 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
   };
   // two rows in flight per warp: rr and rr + ngroups (the ring holds every chunk the
   // rows in flight of all warps can touch; checked by stream_plan's caller)
+  // K = 6144: one warp of the sixteen has no segment and skips the rows
+  const XSeg xs = load_xseg(qx, dx, nb, grp < ngroups ? seg : 0);
   Pos pa = advance(Pos{0, 0, 0u}, grp);
-  for (int rr = grp; rr < nrows; rr += 2 * ngroups, pa = advance(pa, 2 * ngroups)) {
+  for (int rr = grp < ngroups ? grp : nrows; rr < nrows; rr += 2 * ngroups, pa = advance(pa, 2 * ngroups)) {
     const int rb = rr + ngroups;
     const bool has_b = rb < nrows;
     if (!bar_wait(&full[pa.slot], pa.parity)) break;
@@ -414,6 +425,41 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
       finish(rr, pa.slot, pa.ri, va);
       if (has_b) finish(rb, pb.slot, pb.ri, vb);
     }
+  }
+  if (!allreduce) return;
+
+  // ---- cross-GPU sum of this CTA's rows (the same row range on every rank) ----
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");  // all rows staged
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // the peer stores of this CTA before its flags
+    const unsigned slot = blockIdx.x * (unsigned)fz.ar_world + (unsigned)fz.ar_rank;
+    for (int p = 0; p < fz.ar_world; ++p)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(fz.ar_flags[p] + slot), "r"(fz.ar_epoch) : "memory");
+    const unsigned* mine = fz.ar_flags[fz.ar_rank] + blockIdx.x * (unsigned)fz.ar_world;
+    int ok = 1;
+    for (int p = 0; p < fz.ar_world && ok; ++p) {
+      ok = 0;
+      for (uint32_t i = 0; i < kPeerWaitLimit; ++i) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + p) : "memory");
+        if ((int)(v - fz.ar_epoch) >= 0) {  // this call's flag or a later one
+          ok = 1;
+          break;
+        }
+        if (i > 64) __nanosleep(64);
+      }
+    }
+    if (!ok) atomicOr(&g_gemv_fault, 2u);
+    s_ok = ok;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+  if (!s_ok) return;
+  const float* stage = fz.ar_stage[fz.ar_rank] + (size_t)(fz.ar_epoch & 1u) * fz.ar_world * N;
+  for (int rr = threadIdx.x; rr < nrows; rr += kConsumerWarps * 32) {
+    float v = __ldcv(stage + r0 + rr);  // rank 0's rows, then rank 1's, ... (fixed order)
+    for (int p = 1; p < fz.ar_world; ++p) v = __fadd_rn(v, __ldcv(stage + (size_t)p * N + r0 + rr));
+    y[r0 + rr] = fz.residual ? __fadd_rn(res_from_smem ? res_s[rr] : fz.residual[r0 + rr], v) : v;
   }
 }
 

@@ -42,9 +42,26 @@ struct GemvFusion {
   const float* norm_w = nullptr;
   float eps = 0.0f;
   const float* residual = nullptr;
+  // Sum of the output over `ar_world` GPUs (tensor-parallel down projection), fused into
+  // the GEMV: every CTA stores its rows into each rank's staging buffer (peer stores over
+  // NVLink), raises its flag on each rank, waits for the same CTA index of every rank, and
+  // adds the staged rows in rank order.  ar_stage / ar_flags: device arrays of `ar_world`
+  // pointers (this rank's own buffers at index ar_rank); stage[r] holds [2][ar_world][N] f32
+  // (calls alternate halves by epoch parity), flags[r] holds [grid][ar_world] u32.
+  // ar_epoch is a per-call counter starting at 1 and a flag counts once it reaches the
+  // call's epoch, so flags never need resetting; a rank can be at most one call ahead of
+  // a peer's reads (its next reduction waits for that peer's next flag), which the two
+  // staging halves cover.
+  float* const* ar_stage = nullptr;
+  unsigned* const* ar_flags = nullptr;
+  int ar_rank = 0;
+  int ar_world = 1;
+  unsigned ar_epoch = 0;
 };
 // The fused forms need the streaming kernel: M = 1 and K <= this bound.
 constexpr int kFusedMaxK = 8192;
+// CTAs covered by the cross-GPU flag arrays (the streaming kernel runs one per SM).
+constexpr int kAllreduceMaxCtas = 1024;
 cudaError_t launch_gemv_fused(const q8lin_weight& w, const float* x, float* y, const GemvFusion& f, cudaStream_t s);
 
 // Decode GEMV for 1 <= m <= kGemvMaxM.

@@ -14,7 +14,12 @@ The VoxCPM MLP (crates/voxcpm/src/transformer.rs:147-150) is
   unsplit activation row would have;
 * one all-reduce (sum, f32, M x hidden) over the process group (NCCL over NVLink)
   adds the partial outputs.  The summation order differs from the single-GPU CPU
-  path, so results agree within f32 tolerance.
+  path, so results agree within f32 tolerance.  For decode rows (M = 1),
+  ``enable_fused_allreduce()`` replaces the down projection + NCCL all-reduce with one
+  kernel per rank (``q8lin_forward_allreduce``): each CTA pushes its output rows into
+  every rank's staging buffer over NVLink (peer stores into IPC-mapped buffers), raises
+  a flag on every rank, and adds the ranks' rows in rank order once the same CTA of
+  every rank has arrived.
 
 x is replicated: every rank quantizes the same activation rows, so the gate/up
 results are the bit-identical rows the single-GPU path computes.  Everything below
@@ -119,9 +124,69 @@ class SwiGLUMLP:
         """This rank's contribution to y (before the all-reduce)."""
         return self.down.forward(swiglu(self.gate_up.forward(x), self.inter_local), out=out)
 
-    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def _check_group(self) -> None:
         if self.world > 1 and not (torch.distributed.is_available() and torch.distributed.is_initialized()):
             raise Q8LinError(_lib.ERR_INVALID_ARGUMENT, "world > 1 needs an initialized torch.distributed group")
+
+    def enable_fused_allreduce(self) -> None:
+        """Map the staging and flag buffers of every rank (collective: every rank calls
+        it) so that M = 1 forwards run the down projection and the cross-GPU sum as one
+        kernel.  M > 1 keeps the NCCL all-reduce."""
+        self._check_group()
+        if self.world == 1 or getattr(self, "_ar", None) is not None:
+            return
+        L, dev = _lib.lib(), self.device.index
+        sizes = {"stage": L.q8lin_allreduce_stage_bytes(self.hidden, self.world),
+                 "flags": L.q8lin_allreduce_flag_bytes(self.world)}
+        own, handles = {}, {}
+        for name, nbytes in sizes.items():
+            ptr, h = ctypes.c_void_p(), (ctypes.c_uint8 * 64)()
+            check(L.q8lin_peer_alloc(dev, nbytes, ctypes.byref(ptr), h))
+            own[name], handles[name] = ptr, bytes(h)
+        gathered = [None] * self.world
+        torch.distributed.all_gather_object(gathered, handles, group=self.group)
+        opened, ptrs = [], {"stage": [], "flags": []}
+        for r in range(self.world):
+            for name in ("stage", "flags"):
+                if r == self.rank:
+                    ptrs[name].append(own[name].value)
+                    continue
+                p = ctypes.c_void_p()
+                check(L.q8lin_peer_open(dev, gathered[r][name], ctypes.byref(p)))
+                opened.append(p)
+                ptrs[name].append(p.value)
+        self._ar = {"own": own, "opened": opened, "epoch": 0,
+                    "stage": torch.tensor(ptrs["stage"], dtype=torch.int64, device=self.device),
+                    "flags": torch.tensor(ptrs["flags"], dtype=torch.int64, device=self.device)}
+        torch.cuda.synchronize(self.device)
+        torch.distributed.barrier(group=self.group)  # every rank mapped before the first call
+
+    def close_fused_allreduce(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective)."""
+        ar = getattr(self, "_ar", None)
+        if ar is None:
+            return
+        torch.cuda.synchronize(self.device)
+        torch.distributed.barrier(group=self.group)  # no peer still writes into our buffers
+        L, dev = _lib.lib(), self.device.index
+        for p in ar["opened"]:
+            L.q8lin_peer_close(dev, p)
+        for p in ar["own"].values():
+            L.q8lin_peer_free(dev, p)
+        self._ar = None
+
+    def forward(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        self._check_group()
+        ar = getattr(self, "_ar", None)
+        if ar is not None and x.dim() == 2 and x.shape[0] == 1:
+            h = swiglu(self.gate_up.forward(x), self.inter_local)
+            y = out if out is not None else torch.empty((1, self.hidden), dtype=torch.float32, device=self.device)
+            ar["epoch"] += 1
+            check(_lib.lib().q8lin_forward_allreduce(
+                self.down.handle, ctypes.c_void_p(h.data_ptr()), ctypes.c_void_p(y.data_ptr()), 1,
+                ctypes.c_void_p(ar["stage"].data_ptr()), ctypes.c_void_p(ar["flags"].data_ptr()), self.rank,
+                self.world, ar["epoch"], None, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)))
+            return y
         y = self.partial(x, out=out)
         if self.world > 1:
             torch.distributed.all_reduce(y, op=torch.distributed.ReduceOp.SUM, group=self.group)

@@ -148,3 +148,55 @@ def test_tp_nccl_two_gpus(oracle_lib, cuda_device, tmp_path):
     y0, y1 = np.load(tmp_path / "y0.npy"), np.load(tmp_path / "y1.npy")
     assert np.array_equal(y0, y1)
     assert _rel_l2(y0, ref) <= MLP_E2E_REL_L2
+
+
+def _fused_rank(rank, world, port, result_dir):
+    torch.cuda.set_device(rank)
+    torch.distributed.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                         world_size=world, timeout=timedelta(seconds=60),
+                                         device_id=torch.device("cuda", rank))
+    try:
+        hidden, inter = 1024, 2048
+        dev = torch.device("cuda", rank)
+        _, gate, up, down = _weights(600, hidden, inter, 1)
+        mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, rank=rank, world=world)
+        mlp.enable_fused_allreduce()
+        xs, fused, nccl = [], [], []
+        for i in range(6):  # several calls: epochs and both staging halves
+            x = np.random.default_rng(700 + i).standard_normal((1, hidden)).astype(np.float32)
+            xd = torch.from_numpy(x).to(dev)
+            fused.append(mlp.forward(xd).cpu().numpy())
+            y = mlp.partial(xd)
+            torch.distributed.all_reduce(y)
+            nccl.append(y.cpu().numpy())
+            xs.append(x)
+        st = ctypes.c_uint32(0)
+        _lib.check(_lib.lib().q8lin_fault_status(rank, ctypes.byref(st), 1))
+        mlp.close_fused_allreduce()
+        np.savez(os.path.join(result_dir, f"f{rank}.npz"), x=np.concatenate(xs), fused=np.concatenate(fused),
+                 nccl=np.concatenate(nccl), fault=np.array([st.value]))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_fused_gemv_allreduce_matches_nccl(oracle_lib, cuda_device, tmp_path, world):
+    """The down projection with the cross-GPU sum in the same kernel (peer stores over
+    NVLink) against the partial GEMV + NCCL all-reduce: bit-identical for two ranks (a
+    two-term sum does not depend on the order), within f32 tolerance otherwise."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    port = _free_port()
+    torch.multiprocessing.start_processes(_fused_rank, args=(world, port, str(tmp_path)), nprocs=world,
+                                          join=True, start_method="spawn")
+    res = [np.load(tmp_path / f"f{r}.npz") for r in range(world)]
+    _, gate, up, down = _weights(600, 1024, 2048, 1)
+    for r in range(world):
+        assert res[r]["fault"][0] == 0
+        assert np.array_equal(res[r]["fused"], res[0]["fused"])  # every rank holds the same sum
+        if world == 2:
+            assert np.array_equal(res[r]["fused"], res[r]["nccl"])
+        else:
+            assert_close_to_oracle(res[r]["fused"], res[r]["nccl"])
+    ref = oracle_lib.mlp(res[0]["x"], gate, up, down, 1024, 2048, threads=16)
+    assert _rel_l2(res[0]["fused"], ref) <= MLP_E2E_REL_L2
