@@ -60,13 +60,27 @@ size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // tensor-core path with the weights on the MMA's 128-row side; larger batches the f16
 // tensor-core GEMM.
 constexpr int kGemvPathMaxM = 4;
+// 5 <= M <= 16 with K <= 2048: the small-batch streaming kernel (dp4a).  Measured in CUDA
+// graphs on B200 (qkv / o / gate_up at M = 8: 11.4 / 9.3 / 15.7 us against 17.1 / 14.4 /
+// 27.7 us on the int8 tensor-core path); at M <= 4 the register-streaming GEMV stays
+// ahead on the small shapes, and at K > 2048 the per-CTA quantization of every activation
+// row costs more than the tensor-core path's.  Q8LIN_MROW=0 turns it off (comparisons).
+constexpr int kMrowMinM = 5;
+constexpr int kMrowMaxK = 2048;
+bool use_mrow(int64_t m, int64_t k) {
+  static const bool on = [] {
+    const char* v = getenv("Q8LIN_MROW");
+    return !(v && v[0] == '0');
+  }();
+  return on && m >= kMrowMinM && m <= kMrowMaxM && k <= kMrowMaxK && mrow_applies(m, k);
+}
 bool use_gemv(int64_t m, int64_t k) {
   return m >= 1 && m <= kGemvPathMaxM && gemv_smem_bytes((int)m, k) <= kGemvSmemLimit;
 }
 bool use_skinny(int64_t m) { return m > kGemvPathMaxM && m <= kSkinnyMaxM; }
 
 size_t workspace_bytes(int64_t m, int64_t k) {
-  if (m <= 0 || use_gemv(m, k)) return 0;
+  if (m <= 0 || use_mrow(m, k) || use_gemv(m, k)) return 0;
   if (use_skinny(m)) return gemm_skinny_workspace_bytes(m, k);
   return gemm_tc_workspace_bytes(m, k);
 }
@@ -306,6 +320,11 @@ int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
   if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
+  if (use_mrow(m, w->k)) {
+    e = launch_gemv_mrow(*w, x, y, (int)m, s);
+    if (e != cudaSuccess) return cuda_fail(e, "small-batch gemv launch");
+    return Q8LIN_OK;
+  }
   if (use_gemv(m, w->k)) {
     e = launch_gemv(*w, x, y, (int)m, s);
     if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
@@ -330,7 +349,7 @@ int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
 int q8lin_forward(const q8lin_weight* w, const float* x, float* y, int64_t m, q8lin_stream_t stream) {
   int st = validate_weight(w);
   if (st != Q8LIN_OK) return st;
-  if (m <= 0 || use_gemv(m, w->k)) return q8lin_forward_ws(w, x, y, m, nullptr, 0, stream);
+  if (m <= 0 || use_mrow(m, w->k) || use_gemv(m, w->k)) return q8lin_forward_ws(w, x, y, m, nullptr, 0, stream);
   DeviceGuard guard(w->device);
   if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
   void* ws = nullptr;
@@ -361,9 +380,11 @@ int q8lin_fault_status(int device, uint32_t* flags, int clear) {
   if (e == cudaSuccess) e = read_gemv_fault(&g, clear != 0);
   if (e == cudaSuccess) e = read_skinny_fault(&h, clear != 0);
   if (e == cudaSuccess) e = read_attention_fault(&a, clear != 0);
+  unsigned int r = 0;
   if (e == cudaSuccess) e = read_step_fault(&p, clear != 0);
+  if (e == cudaSuccess) e = read_mrow_fault(&r, clear != 0);
   if (e != cudaSuccess) return cuda_fail(e, "read fault word");
-  *flags = f | g | h | a | p;
+  *flags = f | g | h | a | p | r;
   return Q8LIN_OK;
 }
 

@@ -67,6 +67,11 @@ cudaError_t launch_gemv_fused(const q8lin_weight& w, const float* x, float* y, c
 // Decode GEMV for 1 <= m <= kGemvMaxM.
 constexpr int kGemvMaxM = 16;
 size_t gemv_smem_bytes(int m, int64_t k);
+// 2 <= M <= kMrowMaxM streaming GEMV on dp4a (gemv_mrow.cu).
+constexpr int kMrowMaxM = 16;
+bool mrow_applies(int64_t m, int64_t k);
+cudaError_t launch_gemv_mrow(const q8lin_weight& w, const float* x, float* y, int m, cudaStream_t s);
+cudaError_t read_mrow_fault(unsigned int* flags, bool clear);  // bit 1
 cudaError_t launch_gemv(const q8lin_weight& w, const float* x, float* y, int m,
                         cudaStream_t s);
 
