@@ -192,6 +192,14 @@ int q8lin_attention_decode(const float* q, const float* k_cache, const float* v_
 int q8lin_rope_attention_decode(const float* qkv, const int32_t* pos, const float* cos_t, const float* sin_t,
                                 float* k_cache, float* v_cache, int32_t hq, int32_t hkv, int32_t d, int32_t max_t,
                                 float* out, q8lin_stream_t stream);
+/* Q8LIN_ATTN_POS_READY: *pos and the cache rows below it were written before the launch
+ * preceding this one on the stream began (true inside a decode step that starts with an
+ * embedding launch after the previous step's argmax); the kernel then reads them and
+ * starts copying K/V before its dependency wait. */
+#define Q8LIN_ATTN_POS_READY 1u
+int q8lin_rope_attention_decode_ex(const float* qkv, const int32_t* pos, const float* cos_t, const float* sin_t,
+                                   float* k_cache, float* v_cache, int32_t hq, int32_t hkv, int32_t d, int32_t max_t,
+                                   float* out, uint32_t flags, q8lin_stream_t stream);
 /* x[0..n) += y[0..n). */
 int q8lin_add(float* x, const float* y, int64_t n, q8lin_stream_t stream);
 size_t q8lin_argmax_workspace_size(void);

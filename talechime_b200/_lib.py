@@ -73,6 +73,9 @@ SIGNATURES = {
                                               ctypes.c_int32, ctypes.c_int32, _c_p, ctypes.c_size_t, _c_p, _c_p]),
     "q8lin_rope_attention_decode": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_int32, ctypes.c_int32,
                                                    ctypes.c_int32, ctypes.c_int32, _c_p, _c_p]),
+    "q8lin_rope_attention_decode_ex": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_int32,
+                                                      ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_p,
+                                                      ctypes.c_uint32, _c_p]),
     "q8lin_add": (ctypes.c_int, [_c_p, _c_p, _i64, _c_p]),
     "q8lin_peer_alloc": (ctypes.c_int, [ctypes.c_int, ctypes.c_size_t, ctypes.POINTER(_c_p), _c_p]),
     "q8lin_peer_open": (ctypes.c_int, [ctypes.c_int, _c_p, ctypes.POINTER(_c_p)]),

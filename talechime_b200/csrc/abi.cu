@@ -586,6 +586,12 @@ int q8lin_attention_decode(const float* q, const float* k_cache, const float* v_
 int q8lin_rope_attention_decode(const float* qkv, const int32_t* pos, const float* cos_t, const float* sin_t,
                                 float* k_cache, float* v_cache, int32_t hq, int32_t hkv, int32_t d, int32_t max_t,
                                 float* out, q8lin_stream_t stream) {
+  return q8lin_rope_attention_decode_ex(qkv, pos, cos_t, sin_t, k_cache, v_cache, hq, hkv, d, max_t, out, 0u, stream);
+}
+
+int q8lin_rope_attention_decode_ex(const float* qkv, const int32_t* pos, const float* cos_t, const float* sin_t,
+                                   float* k_cache, float* v_cache, int32_t hq, int32_t hkv, int32_t d, int32_t max_t,
+                                   float* out, uint32_t flags, q8lin_stream_t stream) {
   if (d != 128) return fail(Q8LIN_ERR_SHAPE, "rope_attention_decode supports head width 128");
   if (hq <= 0 || hkv <= 0 || hq % hkv || max_t <= 0 || hq > 65535)
     return fail(Q8LIN_ERR_SHAPE, "attention needs hq a positive multiple of hkv and max_t > 0");
@@ -595,7 +601,7 @@ int q8lin_rope_attention_decode(const float* qkv, const int32_t* pos, const floa
   int device = 0;
   cudaGetDevice(&device);
   cudaError_t e = launch_rope_attention(qkv, pos, cos_t, sin_t, k_cache, v_cache, hq, hkv, max_t, out, device,
-                                        reinterpret_cast<cudaStream_t>(stream));
+                                        reinterpret_cast<cudaStream_t>(stream), (flags & Q8LIN_ATTN_POS_READY) != 0);
   if (e != cudaSuccess) return cuda_fail(e, "rope_attention launch");
   return Q8LIN_OK;
 }

@@ -246,7 +246,7 @@ __device__ __forceinline__ void cluster_sync() {
 __global__ void __launch_bounds__(kRaThreads)
 rope_attention_kernel(const float* __restrict__ qkv, const int* __restrict__ pos_dev, const float* __restrict__ cos_t,
                       const float* __restrict__ sin_t, float* __restrict__ kc, float* __restrict__ vc, int Hq, int Hkv,
-                      int max_t, float scale, float* __restrict__ out) {
+                      int max_t, float scale, float* __restrict__ out, int pos_ready) {
   constexpr int D = 128, half = 64;
   extern __shared__ __align__(16) uint8_t ra_raw[];
   RaSmem& sm = *reinterpret_cast<RaSmem*>(ra_raw);
@@ -261,10 +261,17 @@ rope_attention_kernel(const float* __restrict__ qkv, const int* __restrict__ pos
                    "r"(1) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  pdl_wait();
-  // the next linear's CTAs may become resident and fill their weight rings meanwhile
-  // (its own dependency wait still covers this grid's writes)
-  pdl_launch_dependents();
+  // pos_ready: the position and the cache rows below it were written before the
+  // preceding launch began (the decoder's step: the argmax of the previous token is
+  // followed by the embedding kernel, whose dependency wait comes before its trigger), so
+  // they are read and the first K/V chunks are copied before this launch's dependency
+  // wait, overlapping the qkv projection's tail
+  if (!pos_ready) {
+    pdl_wait();
+    // the next linear's CTAs may become resident and fill their weight rings meanwhile
+    // (its own dependency wait still covers this grid's writes)
+    pdl_launch_dependents();
+  }
   const int pos = *pos_dev;
   const int len = pos < 0 ? 0 : min(pos + 1, max_t);  // never past the cache
   const int per = (len + kRaCluster - 1) / kRaCluster;
@@ -292,6 +299,10 @@ rope_attention_kernel(const float* __restrict__ qkv, const int* __restrict__ pos
   __syncthreads();  // barrier init visible before any wait
   if (tid == 0)
     for (int c = 0; c < min(2, nchunks); ++c) issue(c);
+  if (pos_ready) {  // qkv comes from the preceding launch
+    pdl_wait();
+    pdl_launch_dependents();
+  }
   // rotation x*[cos,cos] + [second,first]*[-sin,sin] at the current position
   if (tid < D && pos >= 0 && pos < max_t) {
     const int j = tid < half ? tid : tid - half;
@@ -520,7 +531,8 @@ cudaError_t launch_attention_decode(const float* q, const float* kc, const float
 }
 
 cudaError_t launch_rope_attention(const float* qkv, const int* pos, const float* cos_t, const float* sin_t, float* kc,
-                                  float* vc, int hq, int hkv, int max_t, float* out, int device, cudaStream_t s) {
+                                  float* vc, int hq, int hkv, int max_t, float* out, int device, cudaStream_t s,
+                                  bool pos_ready) {
   static int configured[128] = {0};
   const int dev = (device >= 0 && device < 128) ? device : 0;
   if (!configured[dev]) {
@@ -544,7 +556,8 @@ cudaError_t launch_rope_attention(const float* qkv, const int* pos, const float*
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   const float scale = (float)(1.0 / std::sqrt(128.0));
-  return cudaLaunchKernelEx(&cfg, rope_attention_kernel, qkv, pos, cos_t, sin_t, kc, vc, hq, hkv, max_t, scale, out);
+  return cudaLaunchKernelEx(&cfg, rope_attention_kernel, qkv, pos, cos_t, sin_t, kc, vc, hq, hkv, max_t, scale, out,
+                            pos_ready ? 1 : 0);
 }
 
 cudaError_t read_attention_fault(unsigned int* flags, bool clear) {

@@ -110,7 +110,8 @@ size_t attention_workspace_bytes(int hq, int max_t);
 cudaError_t launch_attention_decode(const float* q, const float* kc, const float* vc, const int* pos, int hq,
                                     int hkv, int max_t, void* ws, float* out, cudaStream_t s);
 cudaError_t launch_rope_attention(const float* qkv, const int* pos, const float* cos_t, const float* sin_t, float* kc,
-                                  float* vc, int hq, int hkv, int max_t, float* out, int device, cudaStream_t s);
+                                  float* vc, int hq, int hkv, int max_t, float* out, int device, cudaStream_t s,
+                                  bool pos_ready);
 cudaError_t read_attention_fault(unsigned int* flags, bool clear);  // bit 3
 cudaError_t launch_add(float* x, const float* y, int64_t n, cudaStream_t s);
 

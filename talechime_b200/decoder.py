@@ -262,9 +262,11 @@ class Q8Decoder:
         check(L.q8lin_embed_rows(self.embed.handle, P(self.token), 1, P(self.x), s))
         for li, w in enumerate(self.layers):
             w["qkv"].forward_fused(self.x, self.qkv, QMatMul.PROLOGUE_RMSNORM, w["attn_norm"], cfg.eps)
-            check(L.q8lin_rope_attention_decode(P(self.qkv), P(self.pos), P(self.cos), P(self.sin),
-                                                P(self.k_cache[li]), P(self.v_cache[li]), cfg.heads, cfg.kv_heads,
-                                                cfg.head_dim, cfg.max_t, P(self.attn), s))
+            # the step starts with the embedding launch after the previous step's argmax,
+            # so the position and the cached rows are ready before this launch's wait
+            check(L.q8lin_rope_attention_decode_ex(P(self.qkv), P(self.pos), P(self.cos), P(self.sin),
+                                                   P(self.k_cache[li]), P(self.v_cache[li]), cfg.heads, cfg.kv_heads,
+                                                   cfg.head_dim, cfg.max_t, P(self.attn), 1, s))
             w["o"].forward_fused(self.attn, self.x, residual=self.x)
             w["gate_up"].forward_fused(self.x, self.gu, QMatMul.PROLOGUE_RMSNORM, w["ffn_norm"], cfg.eps)
             w["down"].forward_fused(self.gu, self.x, QMatMul.PROLOGUE_SWIGLU, residual=self.x)

@@ -104,9 +104,10 @@ def test_attention_decode_matches_softmax(cuda_device, hq, hkv, pos):
         assert np.max(np.abs(got - ref)) <= 2e-5 * np.max(np.abs(ref))
 
 
+@pytest.mark.parametrize("flags", [0, 1])
 @pytest.mark.parametrize("hq,hkv,max_t,pos", [(4, 2, 24, 0), (4, 2, 24, 23), (16, 16, 640, 63), (16, 16, 640, 64),
                                               (16, 2, 640, 300), (8, 8, 200, 199)])
-def test_rope_attention_is_rope_then_attention(cuda_device, hq, hkv, max_t, pos):
+def test_rope_attention_is_rope_then_attention(cuda_device, hq, hkv, max_t, pos, flags):
     """The fused kernel: rotated q/k, the new k/v row appended, softmax over [0, pos]."""
     cfg = DecoderConfig(hidden=256, layers=1, heads=hq, kv_heads=hkv, inter=512, vocab=10, max_t=max_t)
     cos, sin = rope_tables(cfg)
@@ -138,8 +139,9 @@ def test_rope_attention_is_rope_then_attention(cuda_device, hq, hkv, max_t, pos)
         ref[h] = (p / p.sum()) @ v_ref[kh, :pos + 1]
     for _ in range(2):  # the arrival counters are back at zero after a call
         kd, vd = torch.from_numpy(k).to(dev), torch.from_numpy(v).to(dev)
-        _lib.check(L.q8lin_rope_attention_decode(_p(qkv_d), _p(pos_d), _p(cos_d), _p(sin_d), _p(kd), _p(vd), hq, hkv,
-                                                 128, max_t, _p(out), _s()))
+        torch.cuda.synchronize()  # pos and the cache written before the launch (Q8LIN_ATTN_POS_READY)
+        _lib.check(L.q8lin_rope_attention_decode_ex(_p(qkv_d), _p(pos_d), _p(cos_d), _p(sin_d), _p(kd), _p(vd), hq,
+                                                    hkv, 128, max_t, _p(out), flags, _s()))
         torch.cuda.synchronize()
         assert np.max(np.abs(out.cpu().numpy() - ref)) <= 2e-5 * np.max(np.abs(ref))
         assert np.array_equal(kd.cpu().numpy(), k_ref) and np.array_equal(vd.cpu().numpy(), v_ref)
