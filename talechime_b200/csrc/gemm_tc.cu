@@ -18,7 +18,14 @@
 //     packed f32x2 FMAs: no shared-memory traffic and no broadcast of scales per
 //     column, which is what bounds a register-side rescale.
 // TMEM holds two blocks (2 x (I + P) = 512 columns), so the MMAs of block b + 1 run
-// while block b is rescaled.  One CTA owns a 128 (m) x 128 (n) output tile over all K.
+// while block b is rescaled.  One CTA owns a 128 (m) x 128 (n) output tile over a range
+// of K.
+//
+// Split-K: when the output has too few tiles to occupy the SMs (M = 64..256 against a
+// 2048-row weight gives 16-48 tiles), grid.z splits K into ranges of whole scale groups
+// (8 blocks); each CTA writes its partial tile to the workspace and the last CTA of a
+// tile (arrival counter) adds the partials in split order, so the result does not
+// depend on which CTA finishes first.
 //
 // Rings (a stage = 64 K values = 2 blocks):
 //   operand ring (kStages): A f16 tile + B int8 tile + activation scales;
@@ -57,6 +64,8 @@ constexpr int kEpiWarp0 = 2 + kConvWarps;
 constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 512;  // two blocks x (I: kBN columns + P: kBN columns)
 constexpr uint32_t kSpinLimit = 1u << 24;
+constexpr int kSplitMaxCtas = 148;  // tiles x splits bound when splitting (one wave)
+constexpr int kGroupStages = 4;     // stages per 8-block scale group: split boundaries
 
 constexpr int kAStageBytes = kBM * kBK * 2;   // 16 KB f16
 constexpr int kBStageBytes = kBN * kBK * 2;   // 16 KB f16
@@ -82,6 +91,7 @@ struct Smem {
   alignas(8) uint64_t mma_done;             // every MMA this CTA issued has completed
   uint32_t tmem_base;
   int abort;
+  int last;                                 // this CTA adds the split partials of its tile
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -209,7 +219,8 @@ __device__ __forceinline__ uint2 i8x4_to_f16x4(uint32_t w) {
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                     const __grid_constant__ CUtensorMap map_dx, const uint8_t* __restrict__ W, int64_t S, int N,
-                    int K, float* __restrict__ y, int M) {
+                    int K, float* __restrict__ y, int M, int splits, float* __restrict__ part,
+                    unsigned int* __restrict__ cnt) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
@@ -217,7 +228,14 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   const int n0 = blockIdx.x * kBN;
   const int m0 = blockIdx.y * kBM;
   const int nb = K >> 5;
-  const int nstages = (K + kBK - 1) / kBK;
+  const int nstages_all = (K + kBK - 1) / kBK;
+  // this CTA's stages [sbeg, sbeg + nstages): whole scale groups, split blockIdx.z of splits
+  const int ngroups_all = (nstages_all + kGroupStages - 1) / kGroupStages;
+  const int split = blockIdx.z;
+  const int gbeg = (int)(((int64_t)ngroups_all * split) / splits);
+  const int gend = (int)(((int64_t)ngroups_all * (split + 1)) / splits);
+  const int sbeg = gbeg * kGroupStages;
+  const int nstages = min(gend * kGroupStages, nstages_all) - sbeg;
   volatile int* abort = &sm.abort;
 
   if (threadIdx.x == 0) {
@@ -263,10 +281,11 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       for (int s = 0; s < nstages; ++s) {
         const int st = s % kStages;
         if (s >= kStages && !mbar_wait(&sm.consumed[st], ((s / kStages) - 1) & 1, abort)) break;
+        const int gs = sbeg + s;
         mbar_expect_tx(&sm.full[st], kAStageBytes + kB8StageBytes + kDxStageBytes);
-        tma_load_2d(sm.a[st], &map_a, s * kBK, m0, &sm.full[st]);
-        tma_load_2d(sm.b8[st], &map_b, s * kBK, n0, &sm.full[st]);
-        tma_load_2d(sm.dx[st], &map_dx, m0, 2 * s, &sm.full[st]);
+        tma_load_2d(sm.a[st], &map_a, gs * kBK, m0, &sm.full[st]);
+        tma_load_2d(sm.b8[st], &map_b, gs * kBK, n0, &sm.full[st]);
+        tma_load_2d(sm.dx[st], &map_dx, m0, 2 * gs, &sm.full[st]);
         issued = s + 1;
       }
       // Every copy this CTA issued must land before it can exit (on the normal path
@@ -292,7 +311,7 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       // P in the next 128.  K offsets within the 128 B swizzled row: 64 B per block,
       // 32 B per MMA.
       for (int sub = 0; sub < 2; ++sub) {
-        if (2 * s + sub >= nb) break;
+        if (2 * (sbeg + s) + sub >= nb) break;
         if (s >= 1 && !warp_wait(&sm.acc_empty[sub], (s - 1) & 1, abort)) {
           stop = true;
           break;
@@ -319,9 +338,10 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     // groups ahead of the stage being converted, so no global load latency sits on the
     // per-stage path.  A group index below ceil(nb/8) stays inside the row (its scale
     // area is padded to 16 bytes).
+    // Groups are counted from this split's first one (sbeg is a multiple of 4 stages).
     const bool sload = n0 + ct < N;
-    const int ngroups = (nb + 7) / 8;
-    const uint8_t* sbase = W + (size_t)(sload ? n0 + ct : 0) * S + K;
+    const int ngroups = (nb + 7) / 8 - gbeg;
+    const uint8_t* sbase = W + (size_t)(sload ? n0 + ct : 0) * S + K + 16 * (size_t)gbeg;
     const int4 z4 = make_int4(0, 0, 0, 0);
     int4 g0 = (sload && 0 < ngroups) ? ld_stream_v4(sbase) : z4;
     int4 g1 = (sload && 1 < ngroups) ? ld_stream_v4(sbase + 16) : z4;
@@ -362,7 +382,8 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       const int q = s & 3;
       const uint32_t two = (uint32_t)(q == 0 ? g0.x : q == 1 ? g0.y : q == 2 ? g0.z : g0.w);
       *reinterpret_cast<uint16_t*>(sm.sw[bs][0] + soff) = (uint16_t)(two & 0xffffu);
-      *reinterpret_cast<uint16_t*>(sm.sw[bs][1] + soff) = (2 * s + 1 < nb) ? (uint16_t)(two >> 16) : (uint16_t)0;
+      *reinterpret_cast<uint16_t*>(sm.sw[bs][1] + soff) =
+          (2 * (sbeg + s) + 1 < nb) ? (uint16_t)(two >> 16) : (uint16_t)0;
       *reinterpret_cast<__half*>(sm.sx[bs][0] + soff) = __float2half_rn(sm.dx[st][0][ct]);
       *reinterpret_cast<__half*>(sm.sx[bs][1] + soff) = __float2half_rn(sm.dx[st][1][ct]);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -382,7 +403,7 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     for (int j = 0; j < kEpiCols / 2; ++j) acc[j] = make_float2(0.f, 0.f);
     for (int s = 0; s < nstages && !*abort; ++s) {
       for (int sub = 0; sub < 2; ++sub) {
-        if (2 * s + sub >= nb) break;
+        if (2 * (sbeg + s) + sub >= nb) break;
         if (!mbar_wait(&sm.acc_full[sub], s & 1, abort)) break;
         tc_fence_after();
         const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)sub * 2 * kBN + cg * kEpiCols;
@@ -407,19 +428,67 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         }
       }
     }
-    if (mvalid && !*abort) {
-      const int nbase = n0 + cg * kEpiCols;
-      float* yr = y + (size_t)m * N + nbase;
-      if ((N & 3) == 0 && nbase + kEpiCols <= N) {
+    const bool ok = !*abort;
+    const int nbase = n0 + cg * kEpiCols;
+    float* const yr = y + (size_t)m * N + nbase;
+    if (splits == 1) {
+      if (mvalid && ok) {
+        if ((N & 3) == 0 && nbase + kEpiCols <= N) {
+#pragma unroll
+          for (int j = 0; j < kEpiCols / 4; ++j)
+            reinterpret_cast<float4*>(yr)[j] =
+                make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
+        } else {
+#pragma unroll
+          for (int j = 0; j < kEpiCols / 2; ++j) {
+            if (nbase + 2 * j < N) yr[2 * j] = acc[j].x;
+            if (nbase + 2 * j + 1 < N) yr[2 * j + 1] = acc[j].y;
+          }
+        }
+      }
+    } else {
+      // Partial tile [128 rows][128 columns] of this split; the last CTA of the tile
+      // adds the splits in split order and stores y.
+      const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+      const int r = quad * 32 + lane;
+      const float* const tbase = part + (size_t)tile * splits * (kBM * kBN) + r * kBN + cg * kEpiCols;
+      if (ok) {
+        float4* mine = reinterpret_cast<float4*>(part + (size_t)(tile * splits + split) * (kBM * kBN) + r * kBN +
+                                                 cg * kEpiCols);
 #pragma unroll
         for (int j = 0; j < kEpiCols / 4; ++j)
-          reinterpret_cast<float4*>(yr)[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
-      } else {
-#pragma unroll
-        for (int j = 0; j < kEpiCols / 2; ++j) {
-          if (nbase + 2 * j < N) yr[2 * j] = acc[j].x;
-          if (nbase + 2 * j + 1 < N) yr[2 * j + 1] = acc[j].y;
+          mine[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      if (ew == 0 && lane == 0) sm.last = (atomicAdd(&cnt[tile], 1u) == (unsigned)(splits - 1)) ? 1 : 0;
+      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
+      if (sm.last) {
+        __threadfence();
+        if (mvalid && ok) {
+          const bool vec = (N & 3) == 0;
+#pragma unroll 4
+          for (int j = 0; j < kEpiCols / 4; ++j) {
+            float4 t = __ldcg(reinterpret_cast<const float4*>(tbase) + j);
+            for (int sp = 1; sp < splits; ++sp) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(tbase + (size_t)sp * (kBM * kBN)) + j);
+              t.x += v.x;
+              t.y += v.y;
+              t.z += v.z;
+              t.w += v.w;
+            }
+            const int c = nbase + 4 * j;
+            if (vec && c + 4 <= N) {
+              reinterpret_cast<float4*>(yr)[j] = t;
+            } else {
+              if (c < N) yr[4 * j] = t.x;
+              if (c + 1 < N) yr[4 * j + 1] = t.y;
+              if (c + 2 < N) yr[4 * j + 2] = t.z;
+              if (c + 3 < N) yr[4 * j + 3] = t.w;
+            }
+          }
         }
+        if (ew == 0 && lane == 0) cnt[tile] = 0;
       }
     }
   }
@@ -435,12 +504,15 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
 // Quantize x rows for the tensor-core path: f16 integers [M][K] and transposed f32
 // scales dxT[K/32][Mp] (rows padded to Mp = round_up(M, 4) so every row of the scale
 // tensor starts on 16 bytes, as TMA requires).  Thread i handles block b = i / M of
-// row m = i % M, so consecutive threads write consecutive scales.
+// row m = i % M, so consecutive threads write consecutive scales.  Also zeroes the
+// ncnt split-K arrival counters.
 __global__ void quantize_rows_f16t_kernel(const float* __restrict__ x, int M, int Mp, int K,
-                                          __half* __restrict__ qh, float* __restrict__ dxT) {
+                                          __half* __restrict__ qh, float* __restrict__ dxT,
+                                          unsigned int* __restrict__ cnt, int ncnt) {
   const int nb = K >> 5;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   pdl_wait();
+  if (i < ncnt) cnt[i] = 0;
   if (i < (int64_t)M * nb) {
     const int b = (int)(i / M), m = (int)(i % M);
     const float4* src = reinterpret_cast<const float4*>(x + (size_t)m * K + (size_t)b * kQK);
@@ -492,15 +564,28 @@ bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, void* base, uint64_t 
 }
 
 inline int64_t padded_rows(int64_t m) { return (m + 3) / 4 * 4; }
+inline size_t up256(size_t v) { return (v + 255) / 256 * 256; }
+
+// Split count for a (M, N, K) problem: enough CTAs for one wave of kSplitMaxCtas when the
+// output has fewer than half that many tiles, each split at least one scale group.
+int tc_splits(int M, int N, int K) {
+  const int tiles = ((N + kBN - 1) / kBN) * ((M + kBM - 1) / kBM);
+  if (2 * tiles > kSplitMaxCtas) return 1;
+  const int ngroups = ((K + kBK - 1) / kBK + kGroupStages - 1) / kGroupStages;
+  int splits = kSplitMaxCtas / tiles;
+  if (splits > ngroups) splits = ngroups;
+  return splits < 1 ? 1 : splits;
+}
 
 }  // namespace
 
 size_t gemm_tc_smem_bytes() { return sizeof(Smem) + 1024; }
 
+// [qh f16 M x K][dxT f32 nb x Mp][split counters][split partials, one wave of tiles]
 size_t gemm_tc_workspace_bytes(int64_t m, int64_t k) {
-  const size_t qh = ((size_t)(m * k) * 2 + 255) / 256 * 256;
-  const size_t dx = ((size_t)(padded_rows(m) * (k / kQK)) * 4 + 255) / 256 * 256;
-  return qh + dx;
+  const size_t qh = up256((size_t)(m * k) * 2);
+  const size_t dx = up256((size_t)(padded_rows(m) * (k / kQK)) * 4);
+  return qh + dx + up256((size_t)kSplitMaxCtas * 4) + (size_t)kSplitMaxCtas * kBM * kBN * 4;
 }
 
 cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
@@ -508,8 +593,13 @@ cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspac
   const int M = (int)m, K = (int)w.k, N = (int)w.n;
   const int Mp = (int)padded_rows(m);
   const int nb = K / kQK;
-  __half* qh = static_cast<__half*>(workspace);
-  float* dxT = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((size_t)M * K * 2 + 255) / 256 * 256);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  __half* qh = reinterpret_cast<__half*>(ws);
+  float* dxT = reinterpret_cast<float*>(ws + up256((size_t)M * K * 2));
+  unsigned int* cnt = reinterpret_cast<unsigned int*>(ws + up256((size_t)M * K * 2) + up256((size_t)Mp * nb * 4));
+  float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(cnt) + up256((size_t)kSplitMaxCtas * 4));
+  const int splits = tc_splits(M, N, K);
+  const int ncnt = splits > 1 ? kSplitMaxCtas : 0;
 
   CUtensorMap map_a, map_b, map_dx;
   if (!encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, qh, K, M, (uint64_t)K * 2, kBK, kBM,
@@ -526,14 +616,14 @@ cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspac
 
   // 1. quantize
   {
-    const int64_t work = (int64_t)M * nb;
+    const int64_t work = (int64_t)M * nb > ncnt ? (int64_t)M * nb : ncnt;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)((work + 255) / 256));
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, quantize_rows_f16t_kernel, x, M, Mp, K, qh, dxT);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, quantize_rows_f16t_kernel, x, M, Mp, K, qh, dxT, cnt, ncnt);
     if (e != cudaSuccess) return e;
   }
   // 2. tensor-core matmul
@@ -546,14 +636,14 @@ cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspac
     configured[dev] = 1;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
+  cfg.gridDim = dim3((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM), (unsigned)splits);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, gemm_q8_0_tc_kernel, map_a, map_b, map_dx, (const uint8_t*)w.packed, w.row_stride,
-                            N, K, y, M);
+                            N, K, y, M, splits, part, cnt);
 }
 
 cudaError_t read_tc_fault(unsigned int* flags, bool clear) {

@@ -215,6 +215,9 @@ __device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
+// kAllreduce: the cross-GPU sum tail (fz.ar_world > 1) is compiled only into its own
+// instantiation, so the single-GPU kernel keeps its registers and shared memory.
+template <bool kAllreduce>
 __global__ void __launch_bounds__(kStreamThreads, 2)
 gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, const float* __restrict__ x,
                         float* __restrict__ y, int rpc, int slots, const GemvFusion fz) {
@@ -361,10 +364,9 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
   const int seg = warp % nseg, grp = warp / nseg;
   const int nrows = r1 - r0;
   const bool res_from_smem = nrows <= kStreamResRows;
-  const bool allreduce = fz.ar_world > 1;
   // the row's value: written to y, or (cross-GPU sum) staged on every rank
   auto emit = [&](int rr, float v) {
-    if (allreduce) {
+    if constexpr (kAllreduce) {
       const size_t at = ((size_t)(fz.ar_epoch & 1u) * fz.ar_world + fz.ar_rank) * N + r0 + rr;
       for (int p = 0; p < fz.ar_world; ++p) fz.ar_stage[p][at] = v;
     } else {
@@ -407,7 +409,9 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
   };
   // two rows in flight per warp: rr and rr + ngroups (the ring holds every chunk the
   // rows in flight of all warps can touch; checked by stream_plan's caller)
-  // K = 6144: one warp of the sixteen has no segment and skips the rows
+  // K = 6144: one warp of the sixteen has no segment and skips the rows (it stays for the
+  // cross-GPU tail's barriers)
+  if (!kAllreduce && grp >= ngroups) return;
   const XSeg xs = load_xseg(qx, dx, nb, grp < ngroups ? seg : 0);
   Pos pa = advance(Pos{0, 0, 0u}, grp);
   for (int rr = grp < ngroups ? grp : nrows; rr < nrows; rr += 2 * ngroups, pa = advance(pa, 2 * ngroups)) {
@@ -426,8 +430,7 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
       if (has_b) finish(rb, pb.slot, pb.ri, vb);
     }
   }
-  if (!allreduce) return;
-
+  if constexpr (kAllreduce) {
   // ---- cross-GPU sum of this CTA's rows (the same row range on every rank) ----
   asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");  // all rows staged
   __shared__ int s_ok;
@@ -461,6 +464,7 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
     for (int p = 1; p < fz.ar_world; ++p) v = __fadd_rn(v, __ldcv(stage + (size_t)p * N + r0 + rr));
     y[r0 + rr] = fz.residual ? __fadd_rn(res_from_smem ? res_s[rr] : fz.residual[r0 + rr], v) : v;
   }
+  }
 }
 
 // Rows per chunk and ring slots of the M = 1 streaming kernel for this K (slots 0: the
@@ -486,14 +490,14 @@ cudaError_t launch_stream(const q8lin_weight& w, const float* x, float* y, int r
   static int configured_smem[128] = {0};
   const int dev = (w.device >= 0 && w.device < 128) ? w.device : 0;
   if ((int)smem > configured_smem[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_q8_0_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
     // the largest shared-memory carveout, so that two CTAs (this launch's and the
     // next one's) fit on an SM
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemv_q8_0_stream_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                               (int)cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return e;
+    for (const void* fn : {(const void*)gemv_q8_0_stream_kernel<false>, (const void*)gemv_q8_0_stream_kernel<true>}) {
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+      if (e != cudaSuccess) return e;
+    }
     configured_smem[dev] = (int)smem;
   }
   int grid = sm_count(w.device);
@@ -508,8 +512,11 @@ cudaError_t launch_stream(const q8lin_weight& w, const float* x, float* y, int r
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_q8_0_stream_kernel, (const uint8_t*)w.packed, w.row_stride, N, K, x, y, rpc,
-                            slots, fz);
+  if (fz.ar_world > 1)
+    return cudaLaunchKernelEx(&cfg, gemv_q8_0_stream_kernel<true>, (const uint8_t*)w.packed, w.row_stride, N, K, x,
+                              y, rpc, slots, fz);
+  return cudaLaunchKernelEx(&cfg, gemv_q8_0_stream_kernel<false>, (const uint8_t*)w.packed, w.row_stride, N, K, x, y,
+                            rpc, slots, fz);
 }
 
 template <int M>

@@ -1,4 +1,6 @@
-"""The tensor-core batched path (M > 16) against the oracle, plus an exact-integer check."""
+"""The tensor-core batched path (M > 32) against the oracle, plus exact-integer and
+determinism checks.  Outputs with fewer than 75 128x128 tiles split K over CTAs; the
+split count is min(148 // tiles, scale groups of 8 blocks)."""
 import ctypes
 
 import numpy as np
@@ -24,8 +26,12 @@ def _run(oracle_lib, dev, seed, m, k, n):
     (17, 64, 128),      # one stage, partial M tile
     (33, 96, 130),      # odd block count (pad block), partial N tile
     (128, 2048, 256),   # exact tiles
-    (200, 544, 300),    # 17 blocks, ragged everything
-    (64, 6144, 256),    # long K (down projection)
+    (200, 544, 300),    # 17 blocks, ragged everything; 3 splits, the last of one stage
+    (64, 6144, 256),    # long K (down projection): 2 tiles x 24 splits
+    (64, 6144, 2048),   # sweep shape down at M = 64: 16 tiles x 9 splits
+    (64, 2048, 2050),   # 17 tiles x 8 splits, ragged last tile, N not a multiple of 4
+    (96, 2048, 6144),   # sweep shape qkv: 48 tiles x 3 splits
+    (300, 2048, 12288), # 288 tiles: no split
 ])
 def test_tc_matches_oracle(oracle_lib, cuda_device, m, k, n):
     _run(oracle_lib, cuda_device, 300 + m + k + n, m, k, n)
@@ -35,11 +41,13 @@ def test_tc_sweep_shape_m256(oracle_lib, cuda_device):
     _run(oracle_lib, cuda_device, 401, 256, 2048, 2048)
 
 
-def test_tc_integer_products_are_exact(cuda_device):
+@pytest.mark.parametrize("k", [256, 2048])
+def test_tc_integer_products_are_exact(cuda_device, k):
     """Unit scales: x holds integers with |x| <= 127 and amax 127 in every block, so the
-    activation scale is exactly 1 and y is an exact integer dot product."""
+    activation scale is exactly 1 and y is an exact integer dot product (K = 2048 adds
+    the split partials, which are exact integers too)."""
     rng = np.random.default_rng(77)
-    m, k, n = 130, 256, 136
+    m, n = 130, 136
     x = rng.integers(-126, 127, size=(m, k)).astype(np.float32)
     x.reshape(m, k // 32, 32)[:, :, 0] = 127.0  # every block has amax 127 -> d = 1
     qs = rng.integers(-127, 128, size=(n, k // 32, 32), dtype=np.int8)
@@ -51,6 +59,16 @@ def test_tc_integer_products_are_exact(cuda_device):
     ref = x.astype(np.int64) @ qs.reshape(n, k).astype(np.int64).T
     assert np.array_equal(y.astype(np.int64), ref)
     assert np.abs(ref).max() < 2 ** 24  # so the f32 result is exact
+
+
+def test_tc_split_k_is_deterministic(cuda_device):
+    """The last CTA of a tile adds the split partials in split order."""
+    x, w = synth.case(403, 64, 6144, 1024)
+    q = QMatMul.from_gguf_blocks(w, 1024, 6144, device=cuda_device)
+    xt = torch.from_numpy(x).to(cuda_device)
+    first = q.forward(xt).cpu().numpy()
+    for _ in range(5):
+        assert np.array_equal(q.forward(xt).cpu().numpy(), first)
 
 
 def test_tc_fault_word_clear(cuda_device):
