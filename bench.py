@@ -209,9 +209,24 @@ def _device_weight(torch, gen, dev, n, k):
     return QMatMul.from_gguf_blocks(blocks, n, k, device=dev)
 
 
-def time_shape(torch, L, dev, stream, gen, m, k, n, reps, copies=3):
-    """Device time of q8lin_forward_ws for one shape, rotating `copies` weight copies."""
-    mats = [_device_weight(torch, gen, dev, n, k) for _ in range(copies)]
+L2_BYTES = 126 * 1024 * 1024
+
+
+def shape_weights(torch, dev, gen, k, n, copies=None):
+    """Weight copies for time_shape: by default enough that a rotation over them spans
+    twice the L2, so every call reads its weights from HBM."""
+    if copies is None:
+        copies = max(3, -(-2 * L2_BYTES // (n * k * 34 // 32)))
+    return [_device_weight(torch, gen, dev, n, k) for _ in range(copies)]
+
+
+def time_shape(torch, L, dev, stream, gen, m, k, n, reps, mats=None):
+    """Device time of one q8lin_forward_ws call (its quantize and matmul launches) for one
+    shape: `reps` calls captured in a CUDA graph, so host enqueue time does not hide the
+    kernels, each call on the next weight copy of `mats` (shape_weights)."""
+    if mats is None:
+        mats = shape_weights(torch, dev, gen, k, n)
+    copies = len(mats)
     x = torch.randn((m, k), generator=gen, device=dev)
     y = torch.empty((m, n), device=dev)
     need = L.q8lin_workspace_size(mats[0].handle, m)
@@ -228,14 +243,23 @@ def time_shape(torch, L, dev, stream, gen, m, k, n, reps, copies=3):
     for i in range(3):
         run(i)
     torch.cuda.synchronize()
+    calls = max(reps, copies)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(calls):
+            run(i)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    replays = 5
     e0.record(stream)
-    for i in range(reps):
-        run(i)
+    for _ in range(replays):
+        graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
-    del mats
+    ms = e0.elapsed_time(e1) / (replays * calls)
+    del graph
     return ms
 
 
@@ -260,16 +284,19 @@ def run_case(args) -> None:
 
 
 def run_sweep(torch, L, dev, stream) -> list:
-    """M in {1,4,16,64,256,1024} x the four projection shapes."""
+    """M in {1,4,16,64,256,1024} x the four projection shapes; device
+    time per call from CUDA-graph replays over weight copies spanning twice the L2."""
     gen = torch.Generator(device=dev)
     gen.manual_seed(99)
     out = []
     for name, k, n in SHAPES:
+        mats = shape_weights(torch, dev, gen, k, n)
         for m in (1, 4, 16, 64, 256, 1024):
-            ms = time_shape(torch, L, dev, stream, gen, m, k, n, 20)
+            ms = time_shape(torch, L, dev, stream, gen, m, k, n, 20, mats=mats)
             out.append({"shape": name, "m": m, "k": k, "n": n, "us": round(ms * 1e3, 2),
                         "tb_s": round(algorithmic_bytes(m, k, n) / ms / 1e9, 3),
-                        "tflop_s": round(2.0 * m * n * k / ms / 1e9, 1)})
+                        "tflop_s": round(2.0 * m * n * k / ms / 1e9, 1), "weight_copies": len(mats)})
+        del mats
     return out
 
 

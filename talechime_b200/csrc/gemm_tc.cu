@@ -23,9 +23,11 @@
 //
 // Split-K: when the output has too few tiles to occupy the SMs (M = 64..256 against a
 // 2048-row weight gives 16-48 tiles), grid.z splits K into ranges of whole scale groups
-// (8 blocks); each CTA writes its partial tile to the workspace and the last CTA of a
-// tile (arrival counter) adds the partials in split order, so the result does not
-// depend on which CTA finishes first.
+// (8 blocks); each CTA writes the valid rows of its partial tile to the workspace and a
+// second kernel (tc_split_reduce_kernel, all SMs) adds the partials in split order, so
+// the result does not depend on which CTA finishes first.  (Adding them in the last
+// CTA of each tile left one SM doing a tile's whole reduction after the others were
+// done: 22 us of a 36 us call at M = 64, N = K = 2048.)
 //
 // Rings (a stage = 64 K values = 2 blocks):
 //   operand ring (kStages): A f16 tile + B int8 tile + activation scales;
@@ -91,7 +93,6 @@ struct Smem {
   alignas(8) uint64_t mma_done;             // every MMA this CTA issued has completed
   uint32_t tmem_base;
   int abort;
-  int last;                                 // this CTA adds the split partials of its tile
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -219,8 +220,7 @@ __device__ __forceinline__ uint2 i8x4_to_f16x4(uint32_t w) {
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                     const __grid_constant__ CUtensorMap map_dx, const uint8_t* __restrict__ W, int64_t S, int N,
-                    int K, float* __restrict__ y, int M, int splits, float* __restrict__ part,
-                    unsigned int* __restrict__ cnt) {
+                    int K, float* __restrict__ y, int M, int splits, float* __restrict__ part) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
@@ -446,50 +446,15 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
           }
         }
       }
-    } else {
-      // Partial tile [128 rows][128 columns] of this split; the last CTA of the tile
-      // adds the splits in split order and stores y.
+    } else if (mvalid && ok) {
+      // Row r of this split's partial tile [128 rows][128 columns]; rows >= M are not
+      // written (nor read by the reduction).
       const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-      const int r = quad * 32 + lane;
-      const float* const tbase = part + (size_t)tile * splits * (kBM * kBN) + r * kBN + cg * kEpiCols;
-      if (ok) {
-        float4* mine = reinterpret_cast<float4*>(part + (size_t)(tile * splits + split) * (kBM * kBN) + r * kBN +
-                                                 cg * kEpiCols);
+      float4* mine = reinterpret_cast<float4*>(part + (size_t)(tile * splits + split) * (kBM * kBN) +
+                                               (quad * 32 + lane) * kBN + cg * kEpiCols);
 #pragma unroll
-        for (int j = 0; j < kEpiCols / 4; ++j)
-          mine[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
-      }
-      __threadfence();
-      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
-      if (ew == 0 && lane == 0) sm.last = (atomicAdd(&cnt[tile], 1u) == (unsigned)(splits - 1)) ? 1 : 0;
-      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
-      if (sm.last) {
-        __threadfence();
-        if (mvalid && ok) {
-          const bool vec = (N & 3) == 0;
-#pragma unroll 4
-          for (int j = 0; j < kEpiCols / 4; ++j) {
-            float4 t = __ldcg(reinterpret_cast<const float4*>(tbase) + j);
-            for (int sp = 1; sp < splits; ++sp) {
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(tbase + (size_t)sp * (kBM * kBN)) + j);
-              t.x += v.x;
-              t.y += v.y;
-              t.z += v.z;
-              t.w += v.w;
-            }
-            const int c = nbase + 4 * j;
-            if (vec && c + 4 <= N) {
-              reinterpret_cast<float4*>(yr)[j] = t;
-            } else {
-              if (c < N) yr[4 * j] = t.x;
-              if (c + 1 < N) yr[4 * j + 1] = t.y;
-              if (c + 2 < N) yr[4 * j + 2] = t.z;
-              if (c + 3 < N) yr[4 * j + 3] = t.w;
-            }
-          }
-        }
-        if (ew == 0 && lane == 0) cnt[tile] = 0;
-      }
+      for (int j = 0; j < kEpiCols / 4; ++j)
+        mine[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
     }
   }
 
@@ -504,15 +469,12 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
 // Quantize x rows for the tensor-core path: f16 integers [M][K] and transposed f32
 // scales dxT[K/32][Mp] (rows padded to Mp = round_up(M, 4) so every row of the scale
 // tensor starts on 16 bytes, as TMA requires).  Thread i handles block b = i / M of
-// row m = i % M, so consecutive threads write consecutive scales.  Also zeroes the
-// ncnt split-K arrival counters.
+// row m = i % M, so consecutive threads write consecutive scales.
 __global__ void quantize_rows_f16t_kernel(const float* __restrict__ x, int M, int Mp, int K,
-                                          __half* __restrict__ qh, float* __restrict__ dxT,
-                                          unsigned int* __restrict__ cnt, int ncnt) {
+                                          __half* __restrict__ qh, float* __restrict__ dxT) {
   const int nb = K >> 5;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   pdl_wait();
-  if (i < ncnt) cnt[i] = 0;
   if (i < (int64_t)M * nb) {
     const int b = (int)(i / M), m = (int)(i % M);
     const float4* src = reinterpret_cast<const float4*>(x + (size_t)m * K + (size_t)b * kQK);
@@ -530,6 +492,42 @@ __global__ void quantize_rows_f16t_kernel(const float* __restrict__ x, int M, in
       dst[t] = make_uint4(a.x, a.y, c.x, c.y);
     }
     dxT[(size_t)b * Mp + m] = __half2float(dh);
+  }
+  pdl_launch_dependents();
+}
+
+// y[m][n] = sum over splits, in split order, of the partial tiles the split-K matmul
+// wrote: part[tile][split][128][128], tile = (m / 128) * tiles_n + n / 128.  Thread i
+// sums four consecutive columns of one row (tile rows are 128 columns wide, so the
+// four are always inside the partial buffer; only columns < N are stored).
+__global__ void tc_split_reduce_kernel(const float* __restrict__ part, int splits, int M, int N, int tiles_n,
+                                       float* __restrict__ y) {
+  const int quads = tiles_n * (kBN / 4);  // column quads per row, partial-tile padded
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();  // the matmul's partials
+  if (i < (int64_t)M * quads) {
+    const int m = (int)(i / quads), q = (int)(i % quads);
+    const int n = q * 4;
+    const int tile = (m / kBM) * tiles_n + n / kBN;
+    const float4* src = reinterpret_cast<const float4*>(part + (size_t)tile * splits * (kBM * kBN) +
+                                                        (m % kBM) * kBN + n % kBN);
+    float4 t = src[0];
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 v = src[(size_t)sp * (kBM * kBN / 4)];
+      t.x += v.x;
+      t.y += v.y;
+      t.z += v.z;
+      t.w += v.w;
+    }
+    float* yr = y + (size_t)m * N + n;
+    if ((N & 3) == 0 && n + 4 <= N) {
+      *reinterpret_cast<float4*>(yr) = t;
+    } else {
+      if (n < N) yr[0] = t.x;
+      if (n + 1 < N) yr[1] = t.y;
+      if (n + 2 < N) yr[2] = t.z;
+      if (n + 3 < N) yr[3] = t.w;
+    }
   }
   pdl_launch_dependents();
 }
@@ -581,11 +579,11 @@ int tc_splits(int M, int N, int K) {
 
 size_t gemm_tc_smem_bytes() { return sizeof(Smem) + 1024; }
 
-// [qh f16 M x K][dxT f32 nb x Mp][split counters][split partials, one wave of tiles]
+// [qh f16 M x K][dxT f32 nb x Mp][split partials: one wave of 128 x 128 tiles]
 size_t gemm_tc_workspace_bytes(int64_t m, int64_t k) {
   const size_t qh = up256((size_t)(m * k) * 2);
   const size_t dx = up256((size_t)(padded_rows(m) * (k / kQK)) * 4);
-  return qh + dx + up256((size_t)kSplitMaxCtas * 4) + (size_t)kSplitMaxCtas * kBM * kBN * 4;
+  return qh + dx + (size_t)kSplitMaxCtas * kBM * kBN * 4;
 }
 
 cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
@@ -596,10 +594,8 @@ cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspac
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   __half* qh = reinterpret_cast<__half*>(ws);
   float* dxT = reinterpret_cast<float*>(ws + up256((size_t)M * K * 2));
-  unsigned int* cnt = reinterpret_cast<unsigned int*>(ws + up256((size_t)M * K * 2) + up256((size_t)Mp * nb * 4));
-  float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(cnt) + up256((size_t)kSplitMaxCtas * 4));
+  float* part = reinterpret_cast<float*>(ws + up256((size_t)M * K * 2) + up256((size_t)Mp * nb * 4));
   const int splits = tc_splits(M, N, K);
-  const int ncnt = splits > 1 ? kSplitMaxCtas : 0;
 
   CUtensorMap map_a, map_b, map_dx;
   if (!encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, qh, K, M, (uint64_t)K * 2, kBK, kBM,
@@ -616,14 +612,14 @@ cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspac
 
   // 1. quantize
   {
-    const int64_t work = (int64_t)M * nb > ncnt ? (int64_t)M * nb : ncnt;
+    const int64_t work = (int64_t)M * nb;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)((work + 255) / 256));
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, quantize_rows_f16t_kernel, x, M, Mp, K, qh, dxT, cnt, ncnt);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, quantize_rows_f16t_kernel, x, M, Mp, K, qh, dxT);
     if (e != cudaSuccess) return e;
   }
   // 2. tensor-core matmul
@@ -642,8 +638,19 @@ cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspac
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemm_q8_0_tc_kernel, map_a, map_b, map_dx, (const uint8_t*)w.packed, w.row_stride,
-                            N, K, y, M, splits, part, cnt);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_q8_0_tc_kernel, map_a, map_b, map_dx, (const uint8_t*)w.packed,
+                                     w.row_stride, N, K, y, M, splits, part);
+  if (e != cudaSuccess || splits == 1) return e;
+  // 3. split-K: add the partials
+  const int tiles_n = (N + kBN - 1) / kBN;
+  const int64_t work = (int64_t)M * tiles_n * (kBN / 4);
+  cudaLaunchConfig_t rcfg = {};
+  rcfg.gridDim = dim3((unsigned)((work + 255) / 256));
+  rcfg.blockDim = dim3(256);
+  rcfg.stream = s;
+  rcfg.attrs = attr;
+  rcfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&rcfg, tc_split_reduce_kernel, (const float*)part, splits, M, N, tiles_n, y);
 }
 
 cudaError_t read_tc_fault(unsigned int* flags, bool clear) {
