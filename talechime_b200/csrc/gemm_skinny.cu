@@ -15,9 +15,9 @@
 //     of the block read from shared memory.  A CTA that covers the whole K therefore
 //     reproduces the CPU result bit for bit.
 // Split-K: when the weight has too few 128-row tiles to occupy the SMs, grid.y splits
-// the blocks; each CTA writes its partial sums to the workspace and the last CTA of a
-// tile (arrival counter) adds the partials in split order -- deterministic, no atomics
-// on y.
+// the blocks; each CTA writes its partial sums to the workspace and a second kernel
+// (skinny_split_reduce_kernel, all SMs) adds the partials in split order --
+// deterministic, no atomics.
 //
 // A stage is 4 blocks (128 K bytes).  Warp roles (192 threads):
 //   warp 0      TMA producer (weights, activations, activation scales)
@@ -64,7 +64,6 @@ struct Smem {
   alignas(8) uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
-  int last;
 };
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -145,7 +144,6 @@ struct Params {
   uint32_t idesc;
   float* y;
   float* part;       // [tile][split][Np][128] partial sums (splits > 1)
-  unsigned int* cnt; // [tile] arrival counters, zeroed by the quantize kernel
 };
 
 template <int NP>
@@ -300,22 +298,6 @@ gemm_q8_0_skinny_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_
         for (int m = 0; m < NP; ++m)
           if (m < p.M) mine[(size_t)m * kRows + r] = acc[m];
       }
-      __threadfence();
-      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
-      if (warp == 2 && lane == 0) sm.last = (atomicAdd(&p.cnt[tile], 1u) == (unsigned)(p.splits - 1)) ? 1 : 0;
-      asm volatile("bar.sync 1, %0;" ::"r"(kEpiWarps * 32) : "memory");
-      if (sm.last) {
-        __threadfence();
-        if (ok && nvalid) {
-          const float* base = p.part + (size_t)tile * p.splits * NP * kRows;
-          for (int m = 0; m < p.M; ++m) {
-            float sum = base[(size_t)m * kRows + r];
-            for (int sp = 1; sp < p.splits; ++sp) sum += base[((size_t)sp * NP + m) * kRows + r];
-            p.y[(size_t)m * p.N + n] = sum;
-          }
-        }
-        if (warp == 2 && lane == 0) p.cnt[tile] = 0;
-      }
     }
   }
 
@@ -328,13 +310,12 @@ gemm_q8_0_skinny_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_
 }
 
 // Activations -> Q8_0 for the int8 path: qx int8 [M][K] and transposed f32 scales
-// dxT[K/32][Mp] (Mp = M rounded up to 16); also zeroes the split-K arrival counters.
+// dxT[K/32][Mp] (Mp = M rounded up to 16).
 __global__ void quantize_rows_i8t_kernel(const float* __restrict__ x, int M, int Mp, int K, int8_t* __restrict__ qx,
-                                         float* __restrict__ dxT, unsigned int* __restrict__ cnt, int ncnt) {
+                                         float* __restrict__ dxT) {
   const int nb = K >> 5;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   pdl_wait();
-  if (i < ncnt) cnt[i] = 0;
   if (i < (int64_t)Mp * nb) {
     const int b = (int)(i / Mp), m = (int)(i % Mp);
     if (m < M) {
@@ -352,6 +333,23 @@ __global__ void quantize_rows_i8t_kernel(const float* __restrict__ x, int M, int
     } else {
       dxT[(size_t)b * Mp + m] = 0.0f;
     }
+  }
+  pdl_launch_dependents();
+}
+
+// y[m][n] = sum over splits, in split order, of the split-K partials
+// part[tile][split][Np][128] (tile = n / 128); one thread per output, consecutive
+// threads on consecutive n.
+__global__ void skinny_split_reduce_kernel(const float* __restrict__ part, int splits, int Np, int M, int N,
+                                           float* __restrict__ y) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();  // the matmul's partials
+  if (i < (int64_t)M * N) {
+    const int m = (int)(i / N), n = (int)(i % N);
+    const float* src = part + ((size_t)(n / kRows) * splits * Np + m) * kRows + (n % kRows);
+    float sum = src[0];
+    for (int sp = 1; sp < splits; ++sp) sum += src[(size_t)sp * Np * kRows];
+    y[i] = sum;
   }
   pdl_launch_dependents();
 }
@@ -417,8 +415,7 @@ cudaError_t launch_np(const CUtensorMap& mw, const CUtensorMap& mx, const CUtens
 size_t gemm_skinny_workspace_bytes(int64_t m, int64_t k) {
   const int Np = np_of(m);
   const int64_t nb = k / kQK;
-  return up256((size_t)(m * k)) + up256((size_t)Np * nb * 4) + up256((size_t)kMaxCtasWs * 4) +
-         (size_t)kMaxCtasWs * Np * kRows * 4;
+  return up256((size_t)(m * k)) + up256((size_t)Np * nb * 4) + (size_t)kMaxCtasWs * Np * kRows * 4;
 }
 
 cudaError_t launch_gemm_skinny(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
@@ -428,8 +425,7 @@ cudaError_t launch_gemm_skinny(const q8lin_weight& w, const float* x, void* work
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int8_t* qx = reinterpret_cast<int8_t*>(ws);
   float* dxT = reinterpret_cast<float*>(ws + up256((size_t)M * K));
-  unsigned int* cnt = reinterpret_cast<unsigned int*>(ws + up256((size_t)M * K) + up256((size_t)Np * nb * 4));
-  float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(cnt) + up256((size_t)kMaxCtasWs * 4));
+  float* part = reinterpret_cast<float*>(ws + up256((size_t)M * K) + up256((size_t)Np * nb * 4));
 
   const int tiles = (N + kRows - 1) / kRows;
   int splits = (kTargetCtas + tiles / 2) / tiles;
@@ -451,7 +447,6 @@ cudaError_t launch_gemm_skinny(const q8lin_weight& w, const float* x, void* work
   p.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(Np >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
   p.y = y;
   p.part = part;
-  p.cnt = cnt;
 
   CUtensorMap mw, mx, md;
   if (!encode_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, K, N, (uint64_t)w.row_stride, kStageK, kRows,
@@ -465,23 +460,34 @@ cudaError_t launch_gemm_skinny(const q8lin_weight& w, const float* x, void* work
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   {
-    const int64_t work = (int64_t)Np * nb > kMaxCtasWs ? (int64_t)Np * nb : kMaxCtasWs;
+    const int64_t work = (int64_t)Np * nb;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)((work + 255) / 256));
     cfg.blockDim = dim3(256);
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, quantize_rows_i8t_kernel, x, M, Np, K, qx, dxT, cnt, kMaxCtasWs);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, quantize_rows_i8t_kernel, x, M, Np, K, qx, dxT);
     if (e != cudaSuccess) return e;
   }
   const int dev = (w.device >= 0 && w.device < 128) ? w.device : 0;
   static_assert(kMaxNp == 32, "instantiations below cover Np = 16 and 32");
+  cudaError_t e;
   switch (Np) {
-    case 16: return launch_np<16>(mw, mx, md, p, tiles, dev, s);
-    case 32: return launch_np<32>(mw, mx, md, p, tiles, dev, s);
+    case 16: e = launch_np<16>(mw, mx, md, p, tiles, dev, s); break;
+    case 32: e = launch_np<32>(mw, mx, md, p, tiles, dev, s); break;
     default: return cudaErrorInvalidValue;
   }
+  if (e != cudaSuccess || splits == 1) return e;
+  // split-K: add the partials
+  const int64_t outs = (int64_t)M * N;
+  cudaLaunchConfig_t rcfg = {};
+  rcfg.gridDim = dim3((unsigned)((outs + 255) / 256));
+  rcfg.blockDim = dim3(256);
+  rcfg.stream = s;
+  rcfg.attrs = attr;
+  rcfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&rcfg, skinny_split_reduce_kernel, (const float*)part, splits, Np, M, N, y);
 }
 
 cudaError_t read_skinny_fault(unsigned int* flags, bool clear) {
