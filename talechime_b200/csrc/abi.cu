@@ -56,31 +56,47 @@ constexpr size_t kAlign = 256;
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Dispatch by activation rows (crossovers measured on B200 in CUDA graphs): M <= 4
-// streams the weights through the GEMV kernels; 5 <= M <= 32 takes the int8
-// tensor-core path with the weights on the MMA's 128-row side; larger batches the f16
-// tensor-core GEMM.
+// streams the weights through the GEMV kernels, or the small-batch dp4a kernel below;
+// 5 <= M <= 32 takes the small-batch kernel where it wins, else the int8 tensor-core
+// path with the weights on the MMA's 128-row side; larger batches the f16 tensor-core
+// GEMM.
 constexpr int kGemvPathMaxM = 4;
-// 5 <= M <= 16 with K <= 2048: the small-batch streaming kernel (dp4a).  Measured in CUDA
-// graphs on B200 (qkv / o / gate_up at M = 8: 11.4 / 9.3 / 15.7 us against 17.1 / 14.4 /
-// 27.7 us on the int8 tensor-core path); at M <= 4 the register-streaming GEMV stays
-// ahead on the small shapes, and at K > 2048 the per-CTA quantization of every activation
-// row costs more than the tensor-core path's.  Q8LIN_MROW=0 turns it off (comparisons).
-constexpr int kMrowMinM = 5;
-constexpr int kMrowMaxK = 2048;
-bool use_mrow(int64_t m, int64_t k) {
+// The small-batch streaming kernel (dp4a, gemv_mrow.cu) takes, measured on B200 in CUDA
+// graphs over weight copies spanning twice the L2 (us per call, this kernel vs the
+// alternative):
+//   K <= 2048, 5 <= M <= 16  vs int8 tensor cores: qkv M=8 10.2 vs 17.1, o M=8 7.5 vs 14.4;
+//   K <= 2048, M = 3, 4 and N*K >= 8M weights  vs the register-streaming GEMV: qkv M=4
+//     7.1 vs 8.4, gate_up M=4 10.4 vs 12.7 (but o 2048x2048 M=4: 5.0 vs 4.9, and at M = 2
+//     the GEMV keeps o and gate_up: 3.4 vs 4.0, 8.5 vs 8.9);
+//   K > 2048, 2 <= M <= 6  vs the GEMV / int8 tensor cores: down 6144->2048 M=2 7.3 vs 8.1,
+//     M=4 10.0 vs 12.6, M=6 12.8 vs 14.1 (M=8: 15.4 vs 14.3 -- there the per-CTA
+//     quantization of every activation row outgrows the tensor-core path's).
+// Q8LIN_MROW=0 turns it off (comparisons).
+constexpr int kMrowMinM = 5;                     // K <= 2048: from here on
+constexpr int kMrowSmallK = 2048;
+constexpr int kMrowMaxMLongK = 6;                // K > 2048: up to here
+constexpr int64_t kMrowMinWeights = 8 << 20;     // M = 3, 4 at K <= 2048: N*K at least this
+bool use_mrow(int64_t m, int64_t k, int64_t n) {
   static const bool on = [] {
     const char* v = getenv("Q8LIN_MROW");
     return !(v && v[0] == '0');
   }();
-  return on && m >= kMrowMinM && m <= kMrowMaxM && k <= kMrowMaxK && mrow_applies(m, k);
+  if (!on || m < 2 || m > kMrowMaxM) return false;
+  bool pick;
+  if (k > kMrowSmallK) pick = m <= kMrowMaxMLongK;
+  else if (m >= kMrowMinM) pick = true;
+  else pick = m >= 3 && n * k >= kMrowMinWeights;
+  return pick && mrow_applies(m, k);
 }
 bool use_gemv(int64_t m, int64_t k) {
   return m >= 1 && m <= kGemvPathMaxM && gemv_smem_bytes((int)m, k) <= kGemvSmemLimit;
 }
 bool use_skinny(int64_t m) { return m > kGemvPathMaxM && m <= kSkinnyMaxM; }
 
+// (Where the kernel choice depends on N -- M = 3, 4 at K <= 2048 -- both candidates need
+// no workspace, so the size needs only M and K.)
 size_t workspace_bytes(int64_t m, int64_t k) {
-  if (m <= 0 || use_mrow(m, k) || use_gemv(m, k)) return 0;
+  if (m <= 0 || use_mrow(m, k, INT64_MAX / k) || use_gemv(m, k)) return 0;
   if (use_skinny(m)) return gemm_skinny_workspace_bytes(m, k);
   return gemm_tc_workspace_bytes(m, k);
 }
@@ -320,7 +336,7 @@ int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
   if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
-  if (use_mrow(m, w->k)) {
+  if (use_mrow(m, w->k, w->n)) {
     e = launch_gemv_mrow(*w, x, y, (int)m, s);
     if (e != cudaSuccess) return cuda_fail(e, "small-batch gemv launch");
     return Q8LIN_OK;
@@ -349,7 +365,7 @@ int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
 int q8lin_forward(const q8lin_weight* w, const float* x, float* y, int64_t m, q8lin_stream_t stream) {
   int st = validate_weight(w);
   if (st != Q8LIN_OK) return st;
-  if (m <= 0 || use_mrow(m, w->k) || use_gemv(m, w->k)) return q8lin_forward_ws(w, x, y, m, nullptr, 0, stream);
+  if (m <= 0 || use_mrow(m, w->k, w->n) || use_gemv(m, w->k)) return q8lin_forward_ws(w, x, y, m, nullptr, 0, stream);
   DeviceGuard guard(w->device);
   if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
   void* ws = nullptr;

@@ -23,8 +23,8 @@ def _run(oracle_lib, dev, seed, m, k, n):
 @pytest.mark.parametrize("m,k,n", [
     (5, 32, 1),          # one block, one weight row (K <= 2048: the dp4a small-batch kernel)
     (6, 96, 130),        # three blocks, partial row tile (dp4a small-batch kernel)
-    (5, 2080, 1),        # int8 tensor-core path from here on (K > 2048 or M > 16)
-    (6, 2112, 130),      # partial stage, partial row tile
+    (7, 2080, 1),        # int8 tensor-core path from here on (K > 2048 with M > 6, or M > 16)
+    (8, 2112, 130),      # partial stage, partial row tile
     (16, 2048, 2048),    # split-K over 16 row tiles
     (17, 2048, 256),     # Np = 32
     (31, 544, 300),      # Np = 32, ragged
@@ -39,7 +39,7 @@ def test_skinny_matches_oracle(oracle_lib, cuda_device, m, k, n):
 def test_skinny_without_split_is_bit_exact(oracle_lib, cuda_device):
     """150 row tiles fill the SMs without splitting K: one CTA adds every block of a row
     in block order with candle's per-product rounding, so the result is the CPU result.
-    (K = 2080 keeps M = 8 on this path: the dp4a small-batch kernel takes K <= 2048.)"""
+    (K = 2080 keeps M = 8 on this path: past K = 2048 the dp4a small-batch kernel takes M <= 6.)"""
     y, y_ref = _run(oracle_lib, cuda_device, 611, 8, 2080, 128 * 150)
     assert np.array_equal(y, y_ref)
 

@@ -30,6 +30,19 @@ def test_gemv_ragged_shapes(oracle_lib, cuda_device, k, n):
         run_case(oracle_lib, cuda_device, k + n + m, m, k, n)
 
 
+@pytest.mark.parametrize("m,k,n", [
+    (3, 2048, 4096),   # M = 3, 4 with N*K >= 8M weights: the dp4a small-batch kernel
+    (4, 1024, 8200),   # ... ragged N
+    (4, 2048, 2048),   # below 8M weights: the register-streaming GEMV
+    (2, 6144, 300),    # K > 2048, M <= 6: the dp4a small-batch kernel
+    (4, 6144, 130),
+    (6, 4096, 257),
+    (2, 2048, 6144),   # M = 2 at K <= 2048: the register-streaming GEMV
+])
+def test_small_batch_dispatch_shapes(oracle_lib, cuda_device, m, k, n):
+    run_case(oracle_lib, cuda_device, 700 + m + k + n, m, k, n, threads=16)
+
+
 def test_config0_single_linear(oracle_lib, cuda_device):
     # x [1,2048], W 2048x2048 Q8_0, seed 0
     run_case(oracle_lib, cuda_device, 0, 1, 2048, 2048)
