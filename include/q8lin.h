@@ -125,10 +125,10 @@ int q8lin_forward_noalloc(const q8lin_weight* w, const float* x, float* y, int64
 
 /*
  * Device-side fault word of `device` (bit 0: a tensor-core kernel's bounded wait ran
- * out, bit 1: the M = 1 streaming GEMV's, bit 2: the small-batch int8 kernel's, bit 3:
- * the fused attention's, bit 4: the persistent decode step's; the kernel returned early
- * and its output is invalid).  Reads it with a
- * device synchronisation; `clear` resets it.  No counterpart in the reference (candle's
+ * out, bit 1: a streaming GEMV's (M = 1, or the small-batch dp4a kernel), bit 2: the
+ * small-batch int8 tensor-core kernel's, bit 3: the fused attention's, bit 4: the
+ * persistent decode step's; the kernel returned early and its output is invalid).
+ * Reads it with a device synchronisation; `clear` resets it.  No counterpart in the reference (candle's
  * kernels have no bounded waits); this is the library's failure-detection hook.
  */
 int q8lin_fault_status(int device, uint32_t* flags, int clear);
