@@ -36,6 +36,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 SHAPES = [("qkv", 2048, 6144), ("o", 2048, 2048), ("gate_up", 2048, 12288), ("down", 6144, 2048)]
+# the sweep adds the real VoxCPM k/v projection (GQA: 2 x 128 of 2048)
+SWEEP_SHAPES = SHAPES + [("kv", 2048, 256)]
 LAYERS = 28
 METRIC = "Q8_0 matmul achieved HBM TB/s (decode GEMV, M=1)"
 
@@ -284,12 +286,13 @@ def run_case(args) -> None:
 
 
 def run_sweep(torch, L, dev, stream) -> list:
-    """M in {1,4,16,64,256,1024} x the four projection shapes; device
+    """M in {1,4,16,64,256,1024} x the four projection shapes and the
+    real k/v shape (2048 -> 256); device
     time per call from CUDA-graph replays over weight copies spanning twice the L2."""
     gen = torch.Generator(device=dev)
     gen.manual_seed(99)
     out = []
-    for name, k, n in SHAPES:
+    for name, k, n in SWEEP_SHAPES:
         mats = shape_weights(torch, dev, gen, k, n)
         for m in (1, 4, 16, 64, 256, 1024):
             ms = time_shape(torch, L, dev, stream, gen, m, k, n, 20, mats=mats)
@@ -298,6 +301,57 @@ def run_sweep(torch, L, dev, stream) -> list:
                         "tflop_s": round(2.0 * m * n * k / ms / 1e9, 1), "weight_copies": len(mats)})
         del mats
     return out
+
+
+def run_prefill(torch, dist, L, dev, stream, mats, rank: int, world: int, m: int = 4096, reps: int = 3) -> dict:
+    """batched prefill, 4 x 1024 tokens (M = 4096), through the Q8_0
+    linears of the 28 layers (qkv, o, gate_up, down per layer; the M > 32 tensor-core
+    path): one CUDA graph of the 112 calls, device time per pass (CUDA events), max over
+    ranks (one independent replica per GPU).  Attention and the elementwise steps of a
+    prefill are not part of the Q8_0 linear path and are not timed."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4096 + rank)
+    xs = {k: torch.randn((m, k), generator=gen, device=dev) for k in sorted({q.k for q in mats})}
+    ys = {n: torch.empty((m, n), device=dev) for n in sorted({q.n for q in mats})}
+    need = max(L.q8lin_workspace_size(q.handle, m) for q in mats)
+    ws = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    calls = [(q.handle, ctypes.c_void_p(xs[q.k].data_ptr()), ctypes.c_void_p(ys[q.n].data_ptr())) for q in mats]
+
+    def one_pass():
+        for h, xp, yp in calls:
+            st = L.q8lin_forward_ws(h, xp, yp, m, ctypes.c_void_p(ws.data_ptr()), need, sptr)
+            if st:
+                from talechime_b200 import _lib
+                _lib.check(st)
+
+    one_pass()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        one_pass()
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del graph
+    flops = sum(2.0 * m * q.n * q.k for q in mats)
+    return {"config": f"configs[3]: M = {m} (4 x 1024 tokens) through the Q8_0 linears of {len(mats) // 4} layers "
+                      "(qkv 2048->6144, o 2048->2048, gate_up 2048->12288, down 6144->2048), one CUDA graph per pass",
+            "ms_per_pass": ms, "tflops": flops / (ms * 1e-3) / 1e12 * world,
+            "tokens_per_s_linears": world * m / (ms * 1e-3), "calls_per_pass": len(mats),
+            "launches_per_pass": 2 * len(mats)}  # quantize + matmul; no K split at M = 4096
 
 
 def run_tp_mlp(torch, dist, dev, rank: int, world: int, reps: int = 20) -> dict:
@@ -491,6 +545,7 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--no-tp-mlp", action="store_true", help="skip the tensor-parallel MLP measurement")
     ap.add_argument("--no-decoder", action="store_true", help="skip the config-2 decoder tokens/s measurement")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill (M = 4096) linears")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layer copies (28 = the benchmark; fewer only for small profiling captures)")
     ap.add_argument("--case", default=None,
@@ -686,6 +741,8 @@ def main() -> None:
         line["tp_mlp"] = run_tp_mlp(torch, dist, dev, rank, world)
     if not args.no_decoder:
         line["decoder"] = run_decoder(torch, dist, dev, rank, world)
+    if not args.no_prefill:
+        line["prefill"] = run_prefill(torch, dist, L, dev, stream, mats, rank, world)
     if args.sweep and rank == 0:
         line["sweep"] = run_sweep(torch, L, dev, stream)
     if rank == 0:

@@ -32,6 +32,8 @@ def _run(oracle_lib, dev, seed, m, k, n):
     (64, 2048, 2050),   # 17 tiles x 8 splits, ragged last tile, N not a multiple of 4
     (96, 2048, 6144),   # sweep shape qkv: 48 tiles x 3 splits
     (300, 2048, 12288), # 288 tiles: no split
+    (4096, 2048, 256),  # configs[3] prefill rows (M = 4096): 64 tiles x 2 splits
+    (4096, 6144, 200),  # ... down-projection K, ragged N
 ])
 def test_tc_matches_oracle(oracle_lib, cuda_device, m, k, n):
     _run(oracle_lib, cuda_device, 300 + m + k + n, m, k, n)
