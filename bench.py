@@ -287,8 +287,10 @@ def run_case(args) -> None:
 
 def run_sweep(torch, L, dev, stream) -> list:
     """M in {1,4,16,64,256,1024} x the four projection shapes and the
-    real k/v shape (2048 -> 256); device
-    time per call from CUDA-graph replays over weight copies spanning twice the L2."""
+    real k/v shape (2048 -> 256); device time per call from CUDA-graph replays over weight
+    copies spanning twice the L2, and the kernel path that served it."""
+    from talechime_b200 import _lib
+
     gen = torch.Generator(device=dev)
     gen.manual_seed(99)
     out = []
@@ -296,7 +298,8 @@ def run_sweep(torch, L, dev, stream) -> list:
         mats = shape_weights(torch, dev, gen, k, n)
         for m in (1, 4, 16, 64, 256, 1024):
             ms = time_shape(torch, L, dev, stream, gen, m, k, n, 20, mats=mats)
-            out.append({"shape": name, "m": m, "k": k, "n": n, "us": round(ms * 1e3, 2),
+            out.append({"shape": name, "m": m, "k": k, "n": n,
+                        "path": _lib.PATH_NAMES.get(L.q8lin_dispatch_path(m, k, n), "?"), "us": round(ms * 1e3, 2),
                         "tb_s": round(algorithmic_bytes(m, k, n) / ms / 1e9, 3),
                         "tflop_s": round(2.0 * m * n * k / ms / 1e9, 1), "weight_copies": len(mats)})
         del mats

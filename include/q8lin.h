@@ -84,11 +84,28 @@ int q8lin_weight_dequantize(const q8lin_weight* w, float* out, q8lin_stream_t st
 /* Write the weight back in GGUF block layout (device memory, N*K/32*34 bytes). */
 int q8lin_weight_export_gguf(const q8lin_weight* w, void* out_blocks, q8lin_stream_t stream);
 
-/* Workspace bytes q8lin_forward_ws needs for M rows: 0 for M <= 4 (decode GEMV); for
- * 5 <= M <= 32 the int8 activations [M][K], transposed f32 scales and the split-K
- * partial sums of the int8 tensor-core path; for larger M the activations as f16
- * integers [M][K] plus transposed f32 scales.  Regions are 256-byte aligned. */
+/* Workspace bytes q8lin_forward_ws needs for M rows: 0 where a GEMV kernel serves M
+ * (M <= 4, and the small-batch kernel's range, see q8lin_dispatch_path); on the int8
+ * tensor-core path (M <= 32) the int8 activations [M][K], transposed f32 scales and
+ * the split-K partial sums; for larger M the activations as f16 integers [M][K],
+ * transposed f32 scales and one wave of split-K partial tiles.  Regions are 256-byte
+ * aligned. */
 size_t q8lin_workspace_size(const q8lin_weight* w, int64_t m);
+
+/*
+ * The kernel q8lin_forward runs for M rows of an N x K Q8_0 weight (host only, no GPU
+ * needed; -1 for invalid sizes).  The choice follows crossovers measured on B200 in
+ * CUDA graphs.  No counterpart in the reference (candle picks its own CUDA kernels by
+ * M); it makes the dispatch inspectable and testable.
+ */
+enum q8lin_path {
+  Q8LIN_PATH_STREAM_GEMV = 0, /* M = 1: bulk-copy ring, one CTA per SM */
+  Q8LIN_PATH_GEMV = 1,        /* M <= 4: register-streaming GEMV */
+  Q8LIN_PATH_SMALL_BATCH = 2, /* 2 <= M <= 16 where it wins: dp4a against every row */
+  Q8LIN_PATH_INT8_TC = 3,     /* M <= 32: int8 tensor cores, weights on the 128-row side */
+  Q8LIN_PATH_F16_TC = 4       /* M > 32: f16 tensor cores with per-block rescale */
+};
+int q8lin_dispatch_path(int64_t m, int64_t k, int64_t n);
 
 /*
  * y[M][N] = x[M][K] . W^T with candle's CPU Q8_0 semantics: every x row is
@@ -97,7 +114,8 @@ size_t q8lin_workspace_size(const q8lin_weight* w, int64_t m);
  * Replaces: QMatMul::forward for QMatMul::QTensor/Q8_0, called at
  *   crates/voxcpm/src/weights.rs:221 (shape rules as candle's: 2-D [M, K], K == in).
  * x, y: f32 device memory, row-major, contiguous.  M == 0 is a no-op.
- * Uses a library-owned workspace per (device, stream) for M > 16.
+ * Uses a library-owned workspace per (device, stream) where the path needs one
+ * (q8lin_workspace_size > 0).
  */
 int q8lin_forward(const q8lin_weight* w, const float* x, float* y, int64_t m,
                   q8lin_stream_t stream);

@@ -26,6 +26,16 @@ ERR_FORMAT = 9
 ERR_IO = 10
 ERR_NOT_FOUND = 11
 
+# q8lin_dispatch_path results (enum q8lin_path)
+PATH_STREAM_GEMV = 0
+PATH_GEMV = 1
+PATH_SMALL_BATCH = 2
+PATH_INT8_TC = 3
+PATH_F16_TC = 4
+PATH_NAMES = {PATH_STREAM_GEMV: "stream_gemv", PATH_GEMV: "gemv", PATH_SMALL_BATCH: "small_batch_dp4a",
+              PATH_INT8_TC: "int8_tc", PATH_F16_TC: "f16_tc"}
+
+
 class Op(ctypes.Structure):
     """struct q8lin_op (one operation of a persistent decode step)."""
     _fields_ = [("kind", ctypes.c_int32), ("prologue", ctypes.c_int32), ("epilogue", ctypes.c_int32),
@@ -55,6 +65,7 @@ SIGNATURES = {
     "q8lin_weight_dequantize": (ctypes.c_int, [_c_p, _c_p, _c_p]),
     "q8lin_weight_export_gguf": (ctypes.c_int, [_c_p, _c_p, _c_p]),
     "q8lin_workspace_size": (ctypes.c_size_t, [_c_p, _i64]),
+    "q8lin_dispatch_path": (ctypes.c_int, [_i64, _i64, _i64]),
     "q8lin_forward": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p]),
     "q8lin_forward_ws": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p, ctypes.c_size_t, _c_p]),
     "q8lin_reserve_workspace": (ctypes.c_int, [ctypes.c_int, _c_p, _i64, _i64]),

@@ -375,6 +375,15 @@ int q8lin_forward(const q8lin_weight* w, const float* x, float* y, int64_t m, q8
   return q8lin_forward_ws(w, x, y, m, ws, need, stream);
 }
 
+int q8lin_dispatch_path(int64_t m, int64_t k, int64_t n) {
+  if (m <= 0 || k <= 0 || n <= 0 || k % kQK) return -1;
+  // the order of q8lin_forward_ws
+  if (use_mrow(m, k, n)) return Q8LIN_PATH_SMALL_BATCH;
+  if (use_gemv(m, k)) return (m == 1 && stream_applies(k)) ? Q8LIN_PATH_STREAM_GEMV : Q8LIN_PATH_GEMV;
+  if (use_skinny(m)) return Q8LIN_PATH_INT8_TC;
+  return Q8LIN_PATH_F16_TC;
+}
+
 int q8lin_reserve_workspace(int device, q8lin_stream_t stream, int64_t m, int64_t k) {
   if (m < 0 || k <= 0 || k % kQK) return fail(Q8LIN_ERR_SHAPE, "reserve needs m >= 0 and k a positive multiple of 32");
   int st = check_device(device);

@@ -550,6 +550,13 @@ cudaError_t launch_m(const q8lin_weight& w, const float* x, float* y, cudaStream
 
 }  // namespace
 
+// Whether the M = 1 streaming kernel serves K (its ring holds at least two chunks).
+bool stream_applies(int64_t k) {
+  int rpc, slots;
+  stream_plan(k, packed_row_stride(k), &rpc, &slots);
+  return slots > 0;
+}
+
 size_t gemv_smem_bytes(int m, int64_t k) {
   return (((size_t)m * k + 15) / 16) * 16 + (size_t)m * (k / kQK) * sizeof(float);
 }

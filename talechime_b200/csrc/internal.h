@@ -72,6 +72,7 @@ constexpr int kMrowMaxM = 16;
 bool mrow_applies(int64_t m, int64_t k);
 cudaError_t launch_gemv_mrow(const q8lin_weight& w, const float* x, float* y, int m, cudaStream_t s);
 cudaError_t read_mrow_fault(unsigned int* flags, bool clear);  // bit 1
+bool stream_applies(int64_t k);  // M = 1 streaming kernel (gemv.cu) serves this K
 cudaError_t launch_gemv(const q8lin_weight& w, const float* x, float* y, int m,
                         cudaStream_t s);
 

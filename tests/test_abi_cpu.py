@@ -82,3 +82,31 @@ def test_python_surface_rejects_cpu_device():
 
     with pytest.raises(ValueError):
         QMatMul.from_gguf_blocks(np.zeros(34, np.uint8), 1, 32, device="cpu")
+
+
+@pytest.mark.parametrize("m,k,n,path", [
+    (1, 2048, 6144, "stream_gemv"),      # decode: bulk-copy ring
+    (1, 16384, 2048, "gemv"),            # K beyond the ring: register streaming
+    (2, 2048, 6144, "gemv"),             # M = 2 at K <= 2048 keeps the GEMV
+    (2, 6144, 2048, "small_batch_dp4a"), # K > 2048, M <= 6: dp4a kernel
+    (6, 6144, 2048, "small_batch_dp4a"),
+    (7, 6144, 2048, "int8_tc"),          # ... from M = 7 the int8 tensor cores
+    (3, 2048, 4096, "small_batch_dp4a"), # M = 3, 4 with N*K >= 8M weights
+    (4, 2048, 2048, "gemv"),             # ... but not below
+    (5, 2048, 2048, "small_batch_dp4a"), # K <= 2048, 5 <= M <= 16
+    (16, 2048, 12288, "small_batch_dp4a"),
+    (17, 2048, 2048, "int8_tc"),
+    (32, 6144, 2048, "int8_tc"),
+    (33, 2048, 2048, "f16_tc"),
+    (4096, 6144, 2048, "f16_tc"),
+])
+def test_dispatch_follows_measured_crossovers(lib, m, k, n, path):
+    """The kernel q8lin_forward picks, queried on the host (the crossovers were measured
+    on B200 in CUDA graphs; the GPU parity tests cover every path)."""
+    from talechime_b200 import _lib
+    assert _lib.PATH_NAMES[lib.q8lin_dispatch_path(m, k, n)] == path
+
+
+def test_dispatch_rejects_invalid_sizes(lib):
+    for m, k, n in ((0, 32, 1), (1, 33, 1), (1, 32, 0), (-1, 32, 1)):
+        assert lib.q8lin_dispatch_path(m, k, n) == -1
