@@ -736,10 +736,13 @@ def main() -> None:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         v, done, el = cpu_run(threads, args.cpu_budget)
+        v1, done1, el1 = cpu_run(1, args.cpu_budget / 2)
         line["cpu_baseline"] = {
             "value": v, "unit": "TB/s", "cores": threads, "kind": "port",
             "sample": f"{done} projections (qkv/o/gate_up/down of 2 layers, M=1) in {el:.1f} s with the "
-                      f"candle-CPU restatement (oracle/q8_0_oracle.c)"}
+                      f"candle-CPU restatement (oracle/q8_0_oracle.c)",
+            "single_thread": {"value": v1, "unit": "TB/s", "cores": 1,
+                              "sample": f"{done1} projections in {el1:.1f} s, one thread"}}
     if not args.no_tp_mlp:
         line["tp_mlp"] = run_tp_mlp(torch, dist, dev, rank, world)
     if not args.no_decoder:
