@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdlib.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <string>
@@ -39,6 +40,10 @@ int sm_count(int device) {
   }
   return cache[device];
 }
+
+std::atomic<uint64_t> g_wait_limit_ns{1000000000ull};
+
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
 
 bool pdl_enabled() {
   static const bool on = [] {

@@ -44,6 +44,58 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) 
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Time-bounded waits.  %globaltimer counts nanoseconds; a spin in the kernels gives up
+// once the host-set limit (q8lin_set_wait_limit_ns, passed as a kernel argument) has
+// passed, or once another warp of the CTA raised the CTA's abort flag.  Waits for a
+// CTA's own bulk copies before it exits use the fixed kDrainLimitNs instead, so that a
+// tiny limit cannot leave copies in flight into released shared memory.
+constexpr uint64_t kDrainLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ bool mb_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+
+// Wait for the completion of the phase of `bar` with `parity`.  False when `limit_ns`
+// passed first or *abort became non-zero (both checked every 16 polls).
+__device__ __forceinline__ bool mb_wait_ns(uint32_t bar, uint32_t parity, uint64_t limit_ns,
+                                           const volatile int* abort) {
+  if (mb_try(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mb_try(bar, parity)) return true;
+    if ((i & 15u) == 0u) {
+      if (abort && *abort) return false;
+      if (global_ns() - t0 > limit_ns) return false;
+    }
+  }
+}
+
+// 16-byte asynchronous copy global -> shared by the calling thread (L2 only), and its
+// commit / wait groups.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// All but the newest `n` (0..3) of this thread's copy groups have landed.
+__device__ __forceinline__ void cp_async_wait(int n) {
+  switch (n) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+  }
+}
+
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
 __device__ __forceinline__ int dot16(const int4 a, const int4 b, int c) {
@@ -183,11 +235,13 @@ __device__ __forceinline__ float block_term(const uint8_t* row, int K, int blk, 
   return __fmul_rn(__fmul_rn(__int2float_rn(isum), dw), dxs);
 }
 
-__device__ __forceinline__ void seg_dot2(const uint8_t* wa, const uint8_t* wb, bool has_b, int K, int seg,
-                                         const XSeg& xs, float& sa, float& sb) {
+// This lane's share of segment `seg` of two rows: the sum of its two block terms.
+__device__ __forceinline__ void seg_terms2(const uint8_t* wa, const uint8_t* wb, bool has_b, int K, int seg,
+                                           const XSeg& xs, float& ta, float& tb) {
   const int lane = threadIdx.x & 31;
   const int b0 = seg * 64 + lane, b1 = b0 + 32;
-  float ta = 0.0f, tb = 0.0f;
+  ta = 0.0f;
+  tb = 0.0f;
   if (xs.va) {
     ta = block_term(wa, K, b0, xs.a0, xs.a1, xs.da);
     if (has_b) tb = block_term(wb, K, b0, xs.a0, xs.a1, xs.da);
@@ -196,11 +250,21 @@ __device__ __forceinline__ void seg_dot2(const uint8_t* wa, const uint8_t* wb, b
     ta = __fadd_rn(ta, block_term(wa, K, b1, xs.b0, xs.b1, xs.db));
     if (has_b) tb = __fadd_rn(tb, block_term(wb, K, b1, xs.b0, xs.b1, xs.db));
   }
+}
+
+__device__ __forceinline__ void warp_sum2(float& ta, float& tb) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     ta += __shfl_xor_sync(kFull, ta, o);
     tb += __shfl_xor_sync(kFull, tb, o);
   }
+}
+
+__device__ __forceinline__ void seg_dot2(const uint8_t* wa, const uint8_t* wb, bool has_b, int K, int seg,
+                                         const XSeg& xs, float& sa, float& sb) {
+  float ta, tb;
+  seg_terms2(wa, wb, has_b, K, seg, xs, ta, tb);
+  warp_sum2(ta, tb);
   sa = ta;
   sb = tb;
 }

@@ -2,9 +2,9 @@
 //
 // HBM-bound: every launch streams the whole repacked weight (N*K*34/32 bytes) once.
 // Two kernels:
-//   * M = 1 and K <= 8192: gemv_q8_0_stream_kernel (below), one CTA per SM with a
-//     shared-memory ring filled by bulk copies, sized so the next linear's CTA is
-//     co-resident and prefetches its weights while this one computes;
+//   * M = 1 and K <= 8192: gemv_q8_0_stream_kernel (below), one CTA per SM whose warps
+//     stream their rows through private shared-memory rings (cp.async), sized so the
+//     next linear's CTA is co-resident and prefetches its weights while this one runs;
 //   * otherwise gemv_q8_0_kernel: two 512-thread CTAs per SM; CTA c owns the contiguous
 //     weight rows [N*c/G, N*(c+1)/G), its warps take those rows round-robin, and the 32
 //     lanes of a warp stride a row in 16-byte chunks (chunk c = half of block c/2) with
@@ -26,6 +26,11 @@
 //      the warp.  The sum over blocks is a tree, so outputs agree with the
 //      sequential CPU order within f32 summation tolerance.
 // Nothing upstream (x) is read and nothing (y) is written before step 2.
+#include <stdio.h>
+#include <stdlib.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -160,43 +165,50 @@ gemv_q8_0_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K,
 }
 
 // ---------------------------------------------------------------------------------
-// M = 1 streaming GEMV with cross-launch weight prefetch.
+// M = 1 streaming GEMV with cross-launch weight prefetch: every warp streams its own rows
+// through a private shared-memory ring with 16-byte cp.async copies.
 //
-// Geometry: one CTA per SM owning the contiguous rows [r0, r1): 16 consumer warps and
-// one producer warp, at most 56 registers per thread and ~100 KB of shared memory, so
-// two CTAs fit on an SM -- the CTA of the next linear in the stream is resident while
-// this one runs.  The CTA's rows are one contiguous byte range of the packed plane,
-// copied into a shared-memory ring of `rpc`-row chunks with 1-D bulk copies
-// (cp.async.bulk from this GPU's own memory).
+// Geometry (host: stream_geometry): one CTA per SM owning the contiguous rows [r0, r1),
+// 16 warps of which the first `nw` have a ring of `depth` slots; a slot holds `rps`
+// consecutive rows (one contiguous byte range of the packed plane).  Slot j of the CTA
+// belongs to warp j % nw.  At most 64 registers per thread and ~105 KB of shared memory,
+// so two CTAs fit on an SM: the CTA of the next linear in the stream is resident while
+// this one runs and fetches its first slots meanwhile.
+//
+// Why per-warp cp.async: measured on B200, 1-D bulk copies (cp.async.bulk) of one CTA
+// complete one after another (~0.35 us each whatever the number in flight: 2 KB copies
+// stream at 0.86 TB/s, 8 KB ones at 3.4 TB/s), while 16-byte cp.async copies issued by
+// the warps themselves reach 6.9-7.1 TB/s with 16-48 KB in flight per SM.  A warp waits
+// for its own copies (cp.async.wait_group) and consumes its slots in order, so the kernel
+// has no spin wait and no mbarrier.  (The earlier shared ring, where every warp waited
+// on an mbarrier parity only for the chunks holding its rows, let a warp reach the next
+// use of a slot before the current use's copy had landed -- the parity test then passes
+// at once; private rings consumed in order cannot do that.)
 //
 // Order of events:
 //   1. launch_dependents at once: the next linear's CTAs may become resident and start
 //      their own copies while this one computes;
-//   2. producer warp: copies of the first `slots` chunks -- weights are constant, so
-//      they are issued before the dependency wait and overlap the previous linear --
-//      then one refill per chunk whose rows have all been reduced (empty barrier);
-//   3. consumer warps: griddepcontrol.wait, x quantized to Q8_0 in shared memory, then
-//      each warp keeps its 2048-value segment of x (four 16-byte units per lane) and
-//      the block scales in registers.  A row of K values is reduced by
-//      ceil(K / 2048) warps, one segment each, straight from the ring; with several
-//      segments the partial sums meet in shared memory and the last warp to arrive
-//      adds them in segment order.  No CTA-wide barrier per chunk.
+//   2. warps with a ring issue their first `depth` slots -- weights are constant, so this
+//      happens before the dependency wait and overlaps the previous linear;
+//   3. all 16 warps: griddepcontrol.wait, the optional prologue (rms_norm, SwiGLU), x
+//      quantized to Q8_0 in shared memory; warps without a ring leave;
+//   4. a ring warp, per slot: wait for its copies, dot products two rows at a time
+//      (K <= 2048: x held in registers; longer rows read their 2048-value segments of x
+//      from shared memory), refill the slot with the warp's slot `depth` further on, and
+//      the lane of each row writes it (+ residual).
 // Each block term is ((f32(isum) * dw) * dx) rounded per product as candle's scalar
 // vec_dot; sums across blocks are trees, so outputs agree within f32 summation
-// tolerance.  Every wait is bounded: on timeout bit 1 of the fault word is set and the
-// waiting warp stops; the producer waits (bounded) for its last copies before it exits.
-constexpr int kConsumerWarps = 16;
-constexpr int kStreamThreads = (kConsumerWarps + 1) * 32;
+// tolerance.  The cross-GPU tail's wait for the peers is bounded in time
+// (q8lin_set_wait_limit_ns): when it runs out, bit 1 of the fault word is set and the
+// CTA's rows are written as NaN.
+constexpr int kStreamWarps = 16;
+constexpr int kStreamThreads = kStreamWarps * 32;
 constexpr int kRingBytes = 96 * 1024;
-constexpr int kMaxSlots = 16;
-constexpr int kMaxRpc = 4;
-constexpr int kUnitsPerLane = 4;
-constexpr int kSegUnits = 32 * kUnitsPerLane;  // 16-byte units per row segment (2048 values)
-constexpr int kMaxSegs = 4;
-constexpr int kStreamMaxK = kMaxSegs * kSegUnits * 16;
-constexpr uint32_t kWaitLimit = 1u << 24;
-constexpr int kStreamResRows = 512;  // residual rows staged in shared memory
-constexpr uint32_t kPeerWaitLimit = 1u << 20;  // polls of a peer's flag (~1 s with the back-off)
+constexpr int kSlotTargetBytes = 4352;  // two rows of K = 2048
+constexpr int kMaxRps = 16;
+constexpr int kMaxDepth = 4;
+constexpr int kSegValues = 2048;  // x values per warp segment (64 blocks, two per lane)
+constexpr int kStreamMaxK = 8192;  // x preparation: four float4 passes of 512 threads
 
 __device__ unsigned int g_gemv_fault;
 
@@ -204,86 +216,59 @@ __host__ __device__ constexpr int64_t round16(int64_t v) { return (v + 15) / 16 
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    uint32_t ok;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
-    if (ok) return true;
-  }
-  atomicOr(&g_gemv_fault, 2u);
-  return false;
-}
+struct StreamGeo {
+  int rps = 0;         // rows per slot
+  int nw = 0;          // warps with a ring
+  int depth = 0;       // slots per ring
+  int slot_bytes = 0;  // rps * S
+};
 
 // kAllreduce: the cross-GPU sum tail (fz.ar_world > 1) is compiled only into its own
-// instantiation, so the single-GPU kernel keeps its registers and shared memory.
-template <bool kAllreduce>
+// instantiation, so the single-GPU kernel keeps its registers.  kXReg: K <= 2048, the
+// warp's x segment lives in registers.
+template <bool kAllreduce, bool kXReg>
 __global__ void __launch_bounds__(kStreamThreads, 2)
 gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, const float* __restrict__ x,
-                        float* __restrict__ y, int rpc, int slots, const GemvFusion fz) {
+                        float* __restrict__ y, const StreamGeo geo, const GemvFusion fz, uint64_t wait_ns) {
   extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float red[kStreamWarps];
+  __shared__ int s_ok;
   const int nb = K >> 5;
-  const int nunits = K >> 4;  // 16-byte units per row; unit u is half of block u / 2
-  const int nseg = (nunits + kSegUnits - 1) / kSegUnits;  // warps per row
-  const int ngroups = kConsumerWarps / nseg;               // rows in flight
   const int r0 = (int)(((int64_t)N * blockIdx.x) / gridDim.x);
   const int r1 = (int)(((int64_t)N * (blockIdx.x + 1)) / gridDim.x);
-  const int nchunks = (r1 - r0 + rpc - 1) / rpc;
-  const size_t chunk_bytes = (size_t)rpc * S;
-  // [ring | qx: K int8 | dx: nb f32 | part: [slot][row][seg] f32 | cnt: [slot][row] |
-  //  full, empty: kMaxSlots mbarriers each], every region on 16 bytes
-  uint8_t* ring = smem;
-  int8_t* qx = reinterpret_cast<int8_t*>(smem + kRingBytes);
-  float* dx = reinterpret_cast<float*>(smem + kRingBytes + round16(K));
-  float* part = reinterpret_cast<float*>(smem + kRingBytes + round16(K) + round16(4 * nb));
-  int* cnt = reinterpret_cast<int*>(part + kMaxSlots * kMaxRpc * kMaxSegs);
-  uint64_t* full = reinterpret_cast<uint64_t*>(cnt + kMaxSlots * kMaxRpc);
-  uint64_t* empty = full + kMaxSlots;
-  float* res_s = reinterpret_cast<float*>(empty + kMaxSlots);  // [kStreamResRows] residual rows of the CTA
+  const int nrows = r1 - r0;
+  const int rps = geo.rps, nw = geo.nw, depth = geo.depth;
+  const int nslots = (nrows + rps - 1) / rps;
+  // [rings: nw x depth slots | qx: K int8 | dx: nb f32]
+  int8_t* qx = reinterpret_cast<int8_t*>(smem + (size_t)nw * depth * geo.slot_bytes);
+  float* dx = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(qx) + round16(K));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ring = smem + (size_t)warp * depth * geo.slot_bytes;  // this warp's ring (warp < nw)
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < slots; ++i) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&full[i])), "r"(1) : "memory");
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&empty[i])), "r"(rpc * nseg)
-                   : "memory");
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  for (int i = threadIdx.x; i < kMaxSlots * kMaxRpc; i += kStreamThreads) cnt[i] = 0;
-  __syncthreads();
   pdl_launch_dependents();
 
-  if (warp == kConsumerWarps) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      int issued = 0;
-      for (int j = 0; j < nchunks; ++j) {
-        const int slot = j % slots;
-        if (j >= slots && !bar_wait(&empty[slot], (uint32_t)((j / slots - 1) & 1))) break;
-        const int row = r0 + j * rpc;
-        const uint32_t bytes = (uint32_t)(min(rpc, r1 - row) * S);
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&full[slot])),
-                     "r"(bytes) : "memory");
-        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                     ::"r"(smem_u32(ring + (size_t)slot * chunk_bytes)), "l"(W + (size_t)row * S), "r"(bytes),
-                     "r"(smem_u32(&full[slot]))
-                     : "memory");
-        issued = j + 1;
-      }
-      // the copies must land before the CTA's shared memory is released
-      for (int j = (issued > slots ? issued - slots : 0); j < issued; ++j)
-        bar_wait(&full[j % slots], (uint32_t)((j / slots) & 1));
+  // the warp's t-th slot (CTA slot warp + t * nw) into ring position t % depth; one copy
+  // group per slot, empty when the warp has no such slot
+  auto issue = [&](int t) {
+    const int j = warp + t * nw;
+    if (j < nslots) {
+      const int row = j * rps;
+      const int units = (min(rps, nrows - row) * (int)S) >> 4;
+      const uint8_t* src = W + (size_t)(r0 + row) * S;
+      const uint32_t dst = smem_u32(ring + (size_t)(t % depth) * geo.slot_bytes);
+      for (int u = lane; u < units; u += 32) cp_async16(dst + 16u * u, src + 16 * (size_t)u);
     }
-    return;
-  }
+    cp_async_commit();
+  };
+  if (warp < nw)
+    for (int t = 0; t < depth; ++t) issue(t);
 
-  // ---------------- consumers ----------------
+  // ---------------- x -> Q8_0 in shared memory (all 16 warps) ----------------
   {
     // float4 pieces of x, 8 lanes per block; the loads of up to four passes are issued
     // together so K <= 8192 costs one L2 round trip
-    constexpr int kT = kConsumerWarps * 32;
-    constexpr int kQG = 4;
+    constexpr int kT = kStreamThreads;
+    constexpr int kQG = (kStreamMaxK / 4 + kT - 1) / kT;
     const int nquads = nb * 8;
     const float4* x4 = reinterpret_cast<const float4*>(x);
     float4 v[kQG], wn[kQG];
@@ -296,8 +281,6 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
       }
     }
     pdl_wait();
-    if (fz.residual && r1 - r0 <= kStreamResRows && (int)threadIdx.x < r1 - r0)
-      res_s[threadIdx.x] = fz.residual[r0 + threadIdx.x];  // read before any row of this CTA is written
     if (fz.prologue == kPrologueSwiGLU) {
       // x = [gate | up], K values each: the activation is silu(gate) * up
 #pragma unroll
@@ -318,9 +301,8 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
       }
     }
     if (fz.prologue == kPrologueRmsNorm) {
-      // rms_norm over the row: sum of squares across the consumer warps (tree order),
+      // rms_norm over the row: sum of squares across the warps (tree order),
       // m = sqrt(sum/K + eps), x -> (x / m) * w
-      __shared__ float red[kConsumerWarps];
       float sq = 0.0f;
 #pragma unroll
       for (int g = 0; g < kQG; ++g) {
@@ -331,10 +313,10 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
       }
       sq = warp_sum(sq);
       if (lane == 0) red[warp] = sq;
-      asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+      __syncthreads();
       float total = 0.0f;
 #pragma unroll
-      for (int i = 0; i < kConsumerWarps; ++i) total += red[i];
+      for (int i = 0; i < kStreamWarps; ++i) total += red[i];
       const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)K), fz.eps));
 #pragma unroll
       for (int g = 0; g < kQG; ++g) {
@@ -348,7 +330,7 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
     }
 #pragma unroll
     for (int g = 0; g < kQG; ++g) {
-      if (g * kT < nquads) {  // uniform across the warps: every lane shuffles
+      if (g * kT < nquads) {  // uniform across the CTA: every lane shuffles
         const int i = g * kT + threadIdx.x;
         __half dh;
         const int q = quantize_octet(v[g], dh);
@@ -359,147 +341,165 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
       }
     }
   }
-  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");  // consumer warps only
+  __syncthreads();
+  if (warp >= nw) return;
 
-  const int seg = warp % nseg, grp = warp / nseg;
-  const int nrows = r1 - r0;
-  const bool res_from_smem = nrows <= kStreamResRows;
-  // the row's value: written to y, or (cross-GPU sum) staged on every rank
+  // ---------------- rows ----------------
+  const int nseg = (K + kSegValues - 1) / kSegValues;
+  XSeg xs;
+  if constexpr (kXReg) xs = load_xseg(qx, dx, nb, 0);
+  // row value `v` of CTA row `rr` (held by one lane): written to y, or (cross-GPU sum)
+  // staged on every rank
   auto emit = [&](int rr, float v) {
     if constexpr (kAllreduce) {
       const size_t at = ((size_t)(fz.ar_epoch & 1u) * fz.ar_world + fz.ar_rank) * N + r0 + rr;
       for (int p = 0; p < fz.ar_world; ++p) fz.ar_stage[p][at] = v;
     } else {
-      y[r0 + rr] = fz.residual ? __fadd_rn(res_from_smem ? res_s[rr] : fz.residual[r0 + rr], v) : v;
+      y[r0 + rr] = v;
     }
   };
-  // finalize row segment `rr` (chunk slot `slot`, row `ri` in the chunk) and release it
-  auto finish = [&](int rr, int slot, int ri, float v) {
-    if (nseg == 1) {
-      emit(rr, v);
-    } else {
-      float* pr = part + (slot * kMaxRpc + ri) * kMaxSegs;
-      pr[seg] = v;
-      __threadfence_block();
-      if (atomicAdd(&cnt[slot * kMaxRpc + ri], 1) == nseg - 1) {
-        __threadfence_block();
-        float sum = pr[0];
-        for (int q = 1; q < nseg; ++q) sum += pr[q];
-        emit(rr, sum);
-        cnt[slot * kMaxRpc + ri] = 0;
-      }
-    }
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&empty[slot])) : "memory");
-  };
-  // Ring position of a row, advanced incrementally (no division in the loop).
-  struct Pos {
-    int ri, slot;
-    uint32_t parity;
-  };
-  auto advance = [&](Pos p, int rows) {
-    p.ri += rows;
-    while (p.ri >= rpc) {
-      p.ri -= rpc;
-      if (++p.slot == slots) {
-        p.slot = 0;
-        p.parity ^= 1u;
-      }
-    }
-    return p;
-  };
-  // two rows in flight per warp: rr and rr + ngroups (the ring holds every chunk the
-  // rows in flight of all warps can touch; checked by stream_plan's caller)
-  // K = 6144: one warp of the sixteen has no segment and skips the rows (it stays for the
-  // cross-GPU tail's barriers)
-  if (!kAllreduce && grp >= ngroups) return;
-  const XSeg xs = load_xseg(qx, dx, nb, grp < ngroups ? seg : 0);
-  Pos pa = advance(Pos{0, 0, 0u}, grp);
-  for (int rr = grp < ngroups ? grp : nrows; rr < nrows; rr += 2 * ngroups, pa = advance(pa, 2 * ngroups)) {
-    const int rb = rr + ngroups;
-    const bool has_b = rb < nrows;
-    if (!bar_wait(&full[pa.slot], pa.parity)) break;
-    const Pos pb = has_b ? advance(pa, ngroups) : pa;
-    if (has_b && !bar_wait(&full[pb.slot], pb.parity)) break;
-    const uint8_t* wa = ring + (size_t)pa.slot * chunk_bytes + (size_t)pa.ri * S;
-    const uint8_t* wb = ring + (size_t)pb.slot * chunk_bytes + (size_t)pb.ri * S;
-    float va, vb;
-    seg_dot2(wa, wb, has_b, K, seg, xs, va, vb);
-    __syncwarp();
-    if (lane == 0) {
-      finish(rr, pa.slot, pa.ri, va);
-      if (has_b) finish(rb, pb.slot, pb.ri, vb);
-    }
-  }
-  if constexpr (kAllreduce) {
-  // ---- cross-GPU sum of this CTA's rows (the same row range on every rank) ----
-  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");  // all rows staged
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) {
-    __threadfence_system();  // the peer stores of this CTA before its flags
-    const unsigned slot = blockIdx.x * (unsigned)fz.ar_world + (unsigned)fz.ar_rank;
-    for (int p = 0; p < fz.ar_world; ++p)
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(fz.ar_flags[p] + slot), "r"(fz.ar_epoch) : "memory");
-    const unsigned* mine = fz.ar_flags[fz.ar_rank] + blockIdx.x * (unsigned)fz.ar_world;
-    int ok = 1;
-    for (int p = 0; p < fz.ar_world && ok; ++p) {
-      ok = 0;
-      for (uint32_t i = 0; i < kPeerWaitLimit; ++i) {
-        unsigned v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + p) : "memory");
-        if ((int)(v - fz.ar_epoch) >= 0) {  // this call's flag or a later one
-          ok = 1;
-          break;
+  for (int t = 0, j = warp; j < nslots; ++t, j += nw) {
+    cp_async_wait(depth - 1);  // this thread's copies of slot t have landed
+    __syncwarp();              // ... and every lane's
+    const uint8_t* sl = ring + (size_t)(t % depth) * geo.slot_bytes;
+    const int row0 = j * rps;
+    const int rows = min(rps, nrows - row0);
+    // residual rows of the slot, read before anything of the slot is written (the
+    // residual may alias y; row i belongs to lane i)
+    float res = 0.0f;
+    if (!kAllreduce && fz.residual && lane < rows) res = fz.residual[r0 + row0 + lane];
+    float mine = 0.0f;
+    for (int i = 0; i < rows; i += 2) {
+      const bool has_b = i + 1 < rows;
+      const uint8_t* wa = sl + (size_t)i * S;
+      const uint8_t* wb = has_b ? wa + S : wa;
+      float ta, tb;
+      if constexpr (kXReg) {
+        seg_terms2(wa, wb, has_b, K, 0, xs, ta, tb);
+      } else {
+        ta = 0.0f;
+        tb = 0.0f;
+        for (int sg = 0; sg < nseg; ++sg) {
+          const XSeg xsg = load_xseg(qx, dx, nb, sg);
+          float pa, pb;
+          seg_terms2(wa, wb, has_b, K, sg, xsg, pa, pb);
+          ta = __fadd_rn(ta, pa);
+          tb = __fadd_rn(tb, pb);
         }
-        if (i > 64) __nanosleep(64);
       }
+      warp_sum2(ta, tb);
+      if (lane == i) mine = ta;
+      if (lane == i + 1) mine = tb;
     }
-    if (!ok) atomicOr(&g_gemv_fault, 2u);
-    s_ok = ok;
+    __syncwarp();  // every lane is done with the slot before it is refilled
+    issue(t + depth);
+    if (lane < rows) emit(row0 + lane, (!kAllreduce && fz.residual) ? __fadd_rn(res, mine) : mine);
   }
-  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
-  if (!s_ok) return;
-  const float* stage = fz.ar_stage[fz.ar_rank] + (size_t)(fz.ar_epoch & 1u) * fz.ar_world * N;
-  for (int rr = threadIdx.x; rr < nrows; rr += kConsumerWarps * 32) {
-    float v = __ldcv(stage + r0 + rr);  // rank 0's rows, then rank 1's, ... (fixed order)
-    for (int p = 1; p < fz.ar_world; ++p) v = __fadd_rn(v, __ldcv(stage + (size_t)p * N + r0 + rr));
-    y[r0 + rr] = fz.residual ? __fadd_rn(res_from_smem ? res_s[rr] : fz.residual[r0 + rr], v) : v;
-  }
+  cp_async_wait(0);  // no copy of this warp outlives it (the trailing groups are empty)
+  if constexpr (kAllreduce) {
+    // ---- cross-GPU sum of this CTA's rows (the same row range on every rank) ----
+    asm volatile("bar.sync 1, %0;" ::"r"(nw * 32) : "memory");  // all rows staged
+    if (threadIdx.x == 0) {
+      int ok = 1;
+      __threadfence_system();  // the peer stores of this CTA before its flags
+      const unsigned slot = blockIdx.x * (unsigned)fz.ar_world + (unsigned)fz.ar_rank;
+      for (int p = 0; p < fz.ar_world; ++p)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(fz.ar_flags[p] + slot), "r"(fz.ar_epoch) : "memory");
+      const unsigned* mine_f = fz.ar_flags[fz.ar_rank] + blockIdx.x * (unsigned)fz.ar_world;
+      const uint64_t t0 = global_ns();
+      for (int p = 0; p < fz.ar_world && ok; ++p) {
+        for (uint32_t i = 0;; ++i) {
+          unsigned v;
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine_f + p) : "memory");
+          if ((int)(v - fz.ar_epoch) >= 0) break;  // this call's flag or a later one
+          if (global_ns() - t0 > wait_ns) {
+            ok = 0;
+            break;
+          }
+          if (i > 64) __nanosleep(64);
+        }
+      }
+      if (!ok) atomicOr(&g_gemv_fault, 2u);
+      s_ok = ok;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(nw * 32) : "memory");
+    if (!s_ok) {  // a peer never arrived: this CTA's rows read as NaN
+      const float nan = __int_as_float(0x7fc00000);
+      for (int rr = threadIdx.x; rr < nrows; rr += nw * 32) y[r0 + rr] = nan;
+      return;
+    }
+    const float* stage = fz.ar_stage[fz.ar_rank] + (size_t)(fz.ar_epoch & 1u) * fz.ar_world * N;
+    for (int rr = threadIdx.x; rr < nrows; rr += nw * 32) {
+      float v = __ldcv(stage + r0 + rr);  // rank 0's rows, then rank 1's, ... (fixed order)
+      for (int p = 1; p < fz.ar_world; ++p) v = __fadd_rn(v, __ldcv(stage + (size_t)p * N + r0 + rr));
+      y[r0 + rr] = fz.residual ? __fadd_rn(fz.residual[r0 + rr], v) : v;
+    }
   }
 }
 
-// Rows per chunk and ring slots of the M = 1 streaming kernel for this K (slots 0: the
-// kernel does not apply).  Chunks shrink until at least 8 fit in the ring.
-void stream_plan(int64_t k, int64_t S, int* rpc, int* slots) {
-  *rpc = kMaxRpc;
-  *slots = 0;
-  if (k > kStreamMaxK) return;
-  while (*rpc > 1 && kRingBytes / (*rpc * S) < 8) *rpc /= 2;
-  const int64_t s = kRingBytes / (*rpc * S);
-  *slots = s < 2 ? 0 : (int)(s > kMaxSlots ? kMaxSlots : s);
+// Slot geometry of the M = 1 streaming kernel for this K (nw == 0: the kernel does not
+// apply): slots of about two K = 2048 rows, depth 2, as many ring warps as the ~96 KB of
+// ring allow (measured on B200 in CUDA graphs against 1-row slots and deeper rings:
+// 2 rows x 11 warps x depth 2 streams the decode chain fastest at K = 2048, and 1 row x
+// 7 warps x depth 2 at K = 6144).  Q8LIN_STREAM_GEO=rps:nw:depth overrides it where the
+// ring fits (experiments).
+StreamGeo stream_geometry(int64_t k, int64_t S) {
+  StreamGeo g;
+  if (k > kStreamMaxK || k % kQK) return g;
+  int64_t rps = kSlotTargetBytes / S;
+  rps = rps < 1 ? 1 : (rps > kMaxRps ? kMaxRps : rps);
+  int depth = 2;
+  int64_t nw = kRingBytes / (rps * S) / depth;
+  if (nw > kStreamWarps) nw = kStreamWarps;
+  static const int* over = [] {
+    static int v[3] = {0, 0, 0};
+    const char* e = getenv("Q8LIN_STREAM_GEO");
+    if (!e || sscanf(e, "%d:%d:%d", &v[0], &v[1], &v[2]) != 3) v[0] = 0;
+    return v;
+  }();
+  if (over[0] >= 1 && over[0] <= kMaxRps && over[1] >= 1 && over[1] <= kStreamWarps && over[2] >= 2 &&
+      over[2] <= kMaxDepth && (int64_t)over[0] * S * over[1] * over[2] <= kRingBytes) {
+    rps = over[0];
+    nw = over[1];
+    depth = over[2];
+  }
+  if (nw < 1) return g;
+  g.rps = (int)rps;
+  g.nw = (int)nw;
+  g.depth = depth;
+  g.slot_bytes = (int)(rps * S);
+  return g;
 }
 
-size_t stream_smem_bytes(int64_t k) {
-  return (size_t)(kRingBytes + round16(k) + round16(4 * (k / kQK)) + kMaxSlots * kMaxRpc * kMaxSegs * 4 +
-                  kMaxSlots * kMaxRpc * 4 + 2 * kMaxSlots * 8 + kStreamResRows * 4);
+size_t stream_smem_bytes(const StreamGeo& g, int64_t k) {
+  return (size_t)g.nw * g.depth * g.slot_bytes + round16(k) + round16(4 * (k / kQK));
 }
 
-cudaError_t launch_stream(const q8lin_weight& w, const float* x, float* y, int rpc, int slots, cudaStream_t s,
-                          const GemvFusion& fz = GemvFusion()) {
+std::mutex g_attr_mu;
+
+// Opt-in of the dynamic shared memory a kernel needs, once per (device, size); with
+// max_carveout the carveout is set to the maximum so that two CTAs of the streaming
+// kernel fit an SM.
+cudaError_t ensure_smem(const void* fn, int* configured, int device, size_t smem, bool max_carveout) {
+  const int dev = (device >= 0 && device < 128) ? device : 0;
+  std::lock_guard<std::mutex> lock(g_attr_mu);
+  if ((int)smem <= configured[dev]) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess && max_carveout)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess) configured[dev] = (int)smem;
+  return e;
+}
+
+template <bool kAllreduce, bool kXReg>
+cudaError_t launch_stream_t(const q8lin_weight& w, const float* x, float* y, const StreamGeo& g, cudaStream_t s,
+                            const GemvFusion& fz) {
   const int K = (int)w.k, N = (int)w.n;
-  const size_t smem = stream_smem_bytes(K);
-  static int configured_smem[128] = {0};
-  const int dev = (w.device >= 0 && w.device < 128) ? w.device : 0;
-  if ((int)smem > configured_smem[dev]) {
-    // the largest shared-memory carveout, so that two CTAs (this launch's and the
-    // next one's) fit on an SM
-    for (const void* fn : {(const void*)gemv_q8_0_stream_kernel<false>, (const void*)gemv_q8_0_stream_kernel<true>}) {
-      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-      if (e != cudaSuccess) return e;
-    }
-    configured_smem[dev] = (int)smem;
-  }
+  const size_t smem = stream_smem_bytes(g, K);
+  static int configured[128] = {0};
+  auto fn = gemv_q8_0_stream_kernel<kAllreduce, kXReg>;
+  cudaError_t e = ensure_smem((const void*)fn, configured, w.device, smem, true);
+  if (e != cudaSuccess) return e;
   int grid = sm_count(w.device);
   if (grid > N) grid = N;
   cudaLaunchConfig_t cfg = {};
@@ -512,11 +512,15 @@ cudaError_t launch_stream(const q8lin_weight& w, const float* x, float* y, int r
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, fn, (const uint8_t*)w.packed, w.row_stride, N, K, x, y, g, fz, wait_limit_ns());
+}
+
+cudaError_t launch_stream(const q8lin_weight& w, const float* x, float* y, const StreamGeo& g, cudaStream_t s,
+                          const GemvFusion& fz = GemvFusion()) {
+  const bool xreg = w.k <= kSegValues;
   if (fz.ar_world > 1)
-    return cudaLaunchKernelEx(&cfg, gemv_q8_0_stream_kernel<true>, (const uint8_t*)w.packed, w.row_stride, N, K, x,
-                              y, rpc, slots, fz);
-  return cudaLaunchKernelEx(&cfg, gemv_q8_0_stream_kernel<false>, (const uint8_t*)w.packed, w.row_stride, N, K, x, y,
-                            rpc, slots, fz);
+    return xreg ? launch_stream_t<true, true>(w, x, y, g, s, fz) : launch_stream_t<true, false>(w, x, y, g, s, fz);
+  return xreg ? launch_stream_t<false, true>(w, x, y, g, s, fz) : launch_stream_t<false, false>(w, x, y, g, s, fz);
 }
 
 template <int M>
@@ -525,12 +529,9 @@ cudaError_t launch_m(const q8lin_weight& w, const float* x, float* y, cudaStream
   const size_t smem = gemv_smem_bytes(M, K);
   // The dynamic shared-memory opt-in is per device context; remember it per device.
   static int configured_smem[128] = {0};
-  const int dev = (w.device >= 0 && w.device < 128) ? w.device : 0;
-  if ((int)smem > 48 * 1024 && (int)smem > configured_smem[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_q8_0_kernel<M>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > 48 * 1024) {
+    cudaError_t e = ensure_smem((const void*)gemv_q8_0_kernel<M>, configured_smem, w.device, smem, false);
     if (e != cudaSuccess) return e;
-    configured_smem[dev] = (int)smem;
   }
   int grid = 2 * sm_count(w.device);
   if (grid > N) grid = N;
@@ -550,12 +551,8 @@ cudaError_t launch_m(const q8lin_weight& w, const float* x, float* y, cudaStream
 
 }  // namespace
 
-// Whether the M = 1 streaming kernel serves K (its ring holds at least two chunks).
-bool stream_applies(int64_t k) {
-  int rpc, slots;
-  stream_plan(k, packed_row_stride(k), &rpc, &slots);
-  return slots > 0;
-}
+// Whether the M = 1 streaming kernel serves K.
+bool stream_applies(int64_t k) { return stream_geometry(k, packed_row_stride(k)).nw > 0; }
 
 size_t gemv_smem_bytes(int m, int64_t k) {
   return (((size_t)m * k + 15) / 16) * 16 + (size_t)m * (k / kQK) * sizeof(float);
@@ -571,17 +568,15 @@ cudaError_t read_gemv_fault(unsigned int* flags, bool clear) {
 }
 
 cudaError_t launch_gemv_fused(const q8lin_weight& w, const float* x, float* y, const GemvFusion& f, cudaStream_t s) {
-  int rpc, slots;
-  stream_plan(w.k, w.row_stride, &rpc, &slots);
-  if (slots == 0 || w.k > kFusedMaxK) return cudaErrorInvalidValue;
-  return launch_stream(w, x, y, rpc, slots, s, f);
+  const StreamGeo g = stream_geometry(w.k, w.row_stride);
+  if (g.nw == 0 || w.k > kFusedMaxK) return cudaErrorInvalidValue;
+  return launch_stream(w, x, y, g, s, f);
 }
 
 cudaError_t launch_gemv(const q8lin_weight& w, const float* x, float* y, int m, cudaStream_t s) {
   if (m == 1) {
-    int rpc, slots;
-    stream_plan(w.k, w.row_stride, &rpc, &slots);
-    if (slots > 0) return launch_stream(w, x, y, rpc, slots, s);
+    const StreamGeo g = stream_geometry(w.k, w.row_stride);
+    if (g.nw > 0) return launch_stream(w, x, y, g, s);
   }
   switch (m) {
     case 1: return launch_m<1>(w, x, y, s);

@@ -5,6 +5,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 struct q8lin_weight {
@@ -152,6 +153,11 @@ size_t argmax_workspace_bytes();
 cudaError_t launch_argmax(const float* logits, int n, void* ws, int* token, int* pos, cudaStream_t s);
 
 int sm_count(int device);
+
+// Time limit of the kernels' spin waits in nanoseconds (q8lin_set_wait_limit_ns), read
+// when a kernel is launched (or captured) and passed to it as an argument.
+uint64_t wait_limit_ns();
+extern std::atomic<uint64_t> g_wait_limit_ns;
 
 // Programmatic dependent launch on/off (env Q8LIN_PDL=0 turns it off; read once).
 bool pdl_enabled();
