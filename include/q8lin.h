@@ -16,9 +16,13 @@
  *     q8lin_last_error() returns the calling thread's message for the last failure.
  *   - Streams are cudaStream_t passed as void* (NULL = legacy default stream).
  *   - x / y / workspace are device pointers on the weight's device, 16-byte aligned.
- *   - q8lin_forward* never synchronizes the host.  q8lin_forward_ws allocates
- *     nothing; q8lin_forward allocates its workspace on first use for M > 16 (see
- *     q8lin_reserve_workspace to do that before stream capture).
+ *   - q8lin_forward* never synchronize the host and never allocate: the paths that
+ *     need scratch (M > 4 outside the small-batch kernel's range) read it from the
+ *     workspace bound to the weight (q8lin_workspace_create at load time, then
+ *     q8lin_weight_bind_workspace) or from the caller (q8lin_forward_ws), so every
+ *     forward entry point may be captured in a CUDA graph.
+ *   - Kernel spin waits are bounded in time (q8lin_set_wait_limit_ns); a wait that runs
+ *     out sets a bit of the device fault word (q8lin_fault_status).
  */
 #ifndef Q8LIN_H
 #define Q8LIN_H
@@ -30,11 +34,12 @@
 extern "C" {
 #endif
 
-#define Q8LIN_VERSION 1
+#define Q8LIN_VERSION 2
 #define Q8LIN_QK 32          /* values per Q8_0 block */
 #define Q8LIN_BLOCK_BYTES 34 /* GGUF block: f16 d + int8 qs[32] */
 
 typedef struct q8lin_weight q8lin_weight; /* one Q8_0 projection resident on one GPU */
+typedef struct q8lin_workspace q8lin_workspace; /* device scratch of the batched paths */
 typedef void* q8lin_stream_t;             /* cudaStream_t */
 
 enum q8lin_status {
@@ -108,22 +113,39 @@ enum q8lin_path {
 int q8lin_dispatch_path(int64_t m, int64_t k, int64_t n);
 
 /*
+ * Workspace of the batched paths, allocated once (load time) and bound to the weights
+ * that use it, so that q8lin_forward itself allocates nothing -- the reference's capture
+ * rule: only buffers allocated before capture survive a replay
+ * (crates/voxcpm/src/cuda_graph/replay.rs:46-80).
+ * q8lin_workspace_bytes(max_m, max_k): bytes covering every M <= max_m and K <= max_k
+ *   (0 if no path needs scratch there).
+ * q8lin_workspace_create allocates it on `device` (cudaMalloc: call it at load time).
+ * q8lin_weight_bind_workspace(w, ws): q8lin_forward(w, ...) reads ws from then on (NULL
+ *   unbinds).  One workspace may be bound to every weight of a model: calls issued on one
+ *   stream are ordered, calls on different streams that share it race.  Weights do not
+ *   own it: unbind or destroy the weights before destroying the workspace.
+ */
+size_t q8lin_workspace_bytes(int64_t max_m, int64_t max_k);
+int q8lin_workspace_create(int device, int64_t max_m, int64_t max_k, q8lin_workspace** out);
+int q8lin_workspace_destroy(q8lin_workspace* ws);
+int q8lin_workspace_capacity(const q8lin_workspace* ws, size_t* bytes);
+int q8lin_weight_bind_workspace(q8lin_weight* w, q8lin_workspace* ws);
+
+/*
  * y[M][N] = x[M][K] . W^T with candle's CPU Q8_0 semantics: every x row is
  * quantized to Q8_0 blocks (d = amax/127, q = round-half-away(x * (1/d)), d kept
  * as f16), then y = sum over blocks of f32(isum) * f32(dw) * f32(dx) in f32.
  * Replaces: QMatMul::forward for QMatMul::QTensor/Q8_0, called at
  *   crates/voxcpm/src/weights.rs:221 (shape rules as candle's: 2-D [M, K], K == in).
  * x, y: f32 device memory, row-major, contiguous.  M == 0 is a no-op.
- * Uses a library-owned workspace per (device, stream) where the path needs one
- * (q8lin_workspace_size > 0).
+ * Where the path needs scratch (q8lin_workspace_size > 0) it uses the workspace bound to
+ * the weight and returns Q8LIN_ERR_WORKSPACE when none is bound or it is too small.
  */
 int q8lin_forward(const q8lin_weight* w, const float* x, float* y, int64_t m,
                   q8lin_stream_t stream);
-/* As q8lin_forward with a caller-provided workspace; allocates nothing. */
+/* As q8lin_forward with a caller-provided workspace (256-byte aligned). */
 int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
                      void* workspace, size_t workspace_bytes, q8lin_stream_t stream);
-/* Grow the library-owned workspace of (device, stream) to cover M rows of K columns. */
-int q8lin_reserve_workspace(int device, q8lin_stream_t stream, int64_t m, int64_t k);
 
 /*
  * No counterpart in the reference.  The same y = x . W^T for callers that must not
@@ -140,6 +162,17 @@ int q8lin_reserve_workspace(int device, q8lin_stream_t stream, int64_t m, int64_
 #define Q8LIN_NOALLOC_MAX_VALUES 8388608
 int q8lin_forward_noalloc(const q8lin_weight* w, const float* x, float* y, int64_t m,
                           q8lin_stream_t stream);
+
+/*
+ * Time limit of every spin wait inside the kernels, in nanoseconds (default 1 s); it
+ * applies to launches issued -- or captured into a CUDA graph -- after the call.  A wait
+ * that runs out sets its bit of the fault word, and the kernel stops, writes NaN where it
+ * could not compute and returns.  Waits for a kernel's own bulk copies before it exits
+ * keep a fixed 2 s bound.  No counterpart in the reference (candle's kernels do not
+ * spin); the library's failure-detection hook together with q8lin_fault_status.
+ */
+int q8lin_set_wait_limit_ns(uint64_t ns);
+uint64_t q8lin_wait_limit_ns(void);
 
 /*
  * Device-side fault word of `device` (bit 0: a tensor-core kernel's bounded wait ran
@@ -236,7 +269,8 @@ int q8lin_argmax(const float* logits, int64_t n, void* workspace, size_t workspa
  * q8lin_allreduce_stage_bytes(N, world) and one flag buffer of
  * q8lin_allreduce_flag_bytes(world) per rank, allocated with q8lin_peer_alloc (zeroed; its
  * IPC handle, Q8LIN_IPC_HANDLE_BYTES bytes, is exchanged out of band and opened on the other
- * ranks with q8lin_peer_open).  stage_ptrs / flag_ptrs: DEVICE arrays of `world` pointers,
+ * ranks with q8lin_peer_open).  stage_n: the N the staging buffers were sized for (a weight
+ * with more rows is rejected).  stage_ptrs / flag_ptrs: DEVICE arrays of `world` pointers,
  * entry r = rank r's buffer as mapped on this GPU.  epoch: the call count, 1, 2, ... (every
  * rank passes the same value; all ranks must make every call).  A rank that never arrives
  * makes the others time out (fault word bit 1) instead of hanging.
@@ -249,7 +283,7 @@ int q8lin_peer_free(int device, void* ptr);
 size_t q8lin_allreduce_stage_bytes(int64_t n, int32_t world);
 size_t q8lin_allreduce_flag_bytes(int32_t world);
 int q8lin_forward_allreduce(const q8lin_weight* w, const float* x, float* y, int64_t m, void* const* stage_ptrs,
-                            void* const* flag_ptrs, int32_t rank, int32_t world, uint32_t epoch,
+                            void* const* flag_ptrs, int64_t stage_n, int32_t rank, int32_t world, uint32_t epoch,
                             const float* residual, q8lin_stream_t stream);
 
 /*

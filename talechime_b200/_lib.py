@@ -68,7 +68,13 @@ SIGNATURES = {
     "q8lin_dispatch_path": (ctypes.c_int, [_i64, _i64, _i64]),
     "q8lin_forward": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p]),
     "q8lin_forward_ws": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p, ctypes.c_size_t, _c_p]),
-    "q8lin_reserve_workspace": (ctypes.c_int, [ctypes.c_int, _c_p, _i64, _i64]),
+    "q8lin_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
+    "q8lin_workspace_create": (ctypes.c_int, [ctypes.c_int, _i64, _i64, ctypes.POINTER(_c_p)]),
+    "q8lin_workspace_destroy": (ctypes.c_int, [_c_p]),
+    "q8lin_workspace_capacity": (ctypes.c_int, [_c_p, ctypes.POINTER(ctypes.c_size_t)]),
+    "q8lin_weight_bind_workspace": (ctypes.c_int, [_c_p, _c_p]),
+    "q8lin_set_wait_limit_ns": (ctypes.c_int, [ctypes.c_uint64]),
+    "q8lin_wait_limit_ns": (ctypes.c_uint64, []),
     "q8lin_quantize_rows": (ctypes.c_int, [_c_p, _i64, _i64, _c_p, _c_p, _c_p]),
     "q8lin_forward_noalloc": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p]),
     "q8lin_fault_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
@@ -94,8 +100,8 @@ SIGNATURES = {
     "q8lin_peer_free": (ctypes.c_int, [ctypes.c_int, _c_p]),
     "q8lin_allreduce_stage_bytes": (ctypes.c_size_t, [_i64, ctypes.c_int32]),
     "q8lin_allreduce_flag_bytes": (ctypes.c_size_t, [ctypes.c_int32]),
-    "q8lin_forward_allreduce": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, ctypes.c_int32, ctypes.c_int32,
-                                               ctypes.c_uint32, _c_p, _c_p]),
+    "q8lin_forward_allreduce": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, _i64, ctypes.c_int32,
+                                                ctypes.c_int32, ctypes.c_uint32, _c_p, _c_p]),
     "q8lin_step_create": (ctypes.c_int, [ctypes.POINTER(Op), ctypes.c_int32, _c_p, _c_p, ctypes.c_int,
                                          ctypes.POINTER(_c_p)]),
     "q8lin_step_run": (ctypes.c_int, [_c_p, _c_p]),

@@ -6,8 +6,6 @@
 #include <stdlib.h>
 
 #include <atomic>
-#include <map>
-#include <mutex>
 #include <string>
 #include <utility>
 #include <vector>
@@ -58,7 +56,6 @@ namespace {
 constexpr size_t kGemvSmemLimit = 200 * 1024;
 constexpr size_t kAlign = 256;
 
-size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Dispatch by activation rows (crossovers measured on B200 in CUDA graphs): M <= 4
 // streams the weights through the GEMV kernels, or the small-batch dp4a kernel below;
@@ -106,24 +103,22 @@ size_t workspace_bytes(int64_t m, int64_t k) {
   return gemm_tc_workspace_bytes(m, k);
 }
 
-// Makes `device` current for the scope and restores the caller's device.
-class DeviceGuard {
- public:
-  explicit DeviceGuard(int device) {
-    ok_ = cudaGetDevice(&prev_) == cudaSuccess;
-    if (ok_ && prev_ != device) ok_ = cudaSetDevice(device) == cudaSuccess;
-    switched_ = ok_ && prev_ != device;
-  }
-  ~DeviceGuard() {
-    if (switched_) cudaSetDevice(prev_);
-  }
-  bool ok() const { return ok_; }
+int validate_weight(const q8lin_weight* w) {
+  if (!w) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "weight handle is null");
+  if (!w->packed || w->n <= 0 || w->k <= 0) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "weight handle is not initialised");
+  return Q8LIN_OK;
+}
 
- private:
-  int prev_ = 0;
-  bool ok_ = false;
-  bool switched_ = false;
-};
+}  // namespace
+
+DeviceGuard::DeviceGuard(int device) {
+  ok_ = cudaGetDevice(&prev_) == cudaSuccess;
+  if (ok_ && prev_ != device) ok_ = cudaSetDevice(device) == cudaSuccess;
+  switched_ = ok_ && prev_ != device;
+}
+DeviceGuard::~DeviceGuard() {
+  if (switched_) cudaSetDevice(prev_);
+}
 
 int check_device(int device) {
   int count = 0;
@@ -143,44 +138,6 @@ int check_device(int device) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-struct Workspace {
-  void* ptr = nullptr;
-  size_t bytes = 0;
-};
-std::mutex g_ws_mu;
-std::map<std::pair<int, cudaStream_t>, Workspace> g_ws;
-
-// Returns a workspace of at least `need` bytes for (device, stream); grows it with
-// stream-ordered allocation so the old buffer is released after queued work.
-int get_workspace(int device, cudaStream_t s, size_t need, void** out) {
-  std::lock_guard<std::mutex> lock(g_ws_mu);
-  Workspace& ws = g_ws[{device, s}];
-  if (ws.bytes < need) {
-    if (ws.ptr) {
-      cudaError_t e = cudaFreeAsync(ws.ptr, s);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync(workspace)");
-      ws.ptr = nullptr;
-      ws.bytes = 0;
-    }
-    const size_t bytes = align_up(need, 1 << 20);
-    cudaError_t e = cudaMallocAsync(&ws.ptr, bytes, s);
-    if (e != cudaSuccess) {
-      ws.ptr = nullptr;
-      return cuda_fail(e, "cudaMallocAsync(workspace)");
-    }
-    ws.bytes = bytes;
-  }
-  *out = ws.ptr;
-  return Q8LIN_OK;
-}
-
-int validate_weight(const q8lin_weight* w) {
-  if (!w) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "weight handle is null");
-  if (!w->packed || w->n <= 0 || w->k <= 0) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "weight handle is not initialised");
-  return Q8LIN_OK;
-}
-
-}  // namespace
 }  // namespace q8lin
 
 using namespace q8lin;
@@ -370,15 +327,80 @@ int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
 int q8lin_forward(const q8lin_weight* w, const float* x, float* y, int64_t m, q8lin_stream_t stream) {
   int st = validate_weight(w);
   if (st != Q8LIN_OK) return st;
-  if (m <= 0 || use_mrow(m, w->k, w->n) || use_gemv(m, w->k)) return q8lin_forward_ws(w, x, y, m, nullptr, 0, stream);
-  DeviceGuard guard(w->device);
-  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
-  void* ws = nullptr;
+  if (m <= 0 || m > (int64_t)1 << 24) return q8lin_forward_ws(w, x, y, m, nullptr, 0, stream);
   const size_t need = workspace_bytes(m, w->k);
-  st = get_workspace(w->device, reinterpret_cast<cudaStream_t>(stream), need, &ws);
-  if (st != Q8LIN_OK) return st;
-  return q8lin_forward_ws(w, x, y, m, ws, need, stream);
+  if (need == 0) return q8lin_forward_ws(w, x, y, m, nullptr, 0, stream);
+  const q8lin_workspace* ws = w->ws;
+  if (!ws || ws->bytes < need)
+    return fail(Q8LIN_ERR_WORKSPACE, "M=" + std::to_string(m) + " needs a workspace of " + std::to_string(need) +
+                                         " bytes; bind one with q8lin_weight_bind_workspace (q8lin_workspace_create "
+                                         "sized for the largest M) or call q8lin_forward_ws");
+  if (ws->device != w->device) return fail(Q8LIN_ERR_DEVICE, "the bound workspace lives on another device");
+  return q8lin_forward_ws(w, x, y, m, ws->ptr, ws->bytes, stream);
 }
+
+size_t q8lin_workspace_bytes(int64_t max_m, int64_t max_k) {
+  if (max_m <= 0 || max_k <= 0 || max_k % kQK || max_m > (int64_t)1 << 24 || max_k > (int64_t)1 << 24) return 0;
+  // the int8 tensor-core path up to M = 32, the f16 path above it: each grows with M and K
+  const size_t b = workspace_bytes(max_m < kSkinnyMaxM ? max_m : kSkinnyMaxM, max_k);
+  const size_t t = workspace_bytes(max_m, max_k);
+  return t > b ? t : b;
+}
+
+int q8lin_workspace_create(int device, int64_t max_m, int64_t max_k, q8lin_workspace** out) {
+  if (!out) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "out is null");
+  *out = nullptr;
+  if (max_m <= 0 || max_k <= 0 || max_k % kQK || max_m > (int64_t)1 << 24 || max_k > (int64_t)1 << 24)
+    return fail(Q8LIN_ERR_SHAPE, "a workspace needs 0 < max_m <= 2^24 and max_k a positive multiple of 32 <= 2^24");
+  int st = check_device(device);
+  if (st != Q8LIN_OK) return st;
+  DeviceGuard guard(device);
+  if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
+  q8lin_workspace* ws = new q8lin_workspace();
+  ws->device = device;
+  ws->bytes = q8lin_workspace_bytes(max_m, max_k);
+  if (ws->bytes > 0) {
+    cudaError_t e = cudaMalloc(&ws->ptr, ws->bytes);
+    if (e != cudaSuccess) {
+      delete ws;
+      return cuda_fail(e, "cudaMalloc(workspace)");
+    }
+  }
+  *out = ws;
+  return Q8LIN_OK;
+}
+
+int q8lin_workspace_destroy(q8lin_workspace* ws) {
+  if (!ws) return Q8LIN_OK;
+  DeviceGuard guard(ws->device);
+  cudaError_t e = ws->ptr ? cudaFree(ws->ptr) : cudaSuccess;
+  delete ws;
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFree(workspace)");
+  return Q8LIN_OK;
+}
+
+int q8lin_workspace_capacity(const q8lin_workspace* ws, size_t* bytes) {
+  if (!ws || !bytes) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "workspace and bytes must be non-null");
+  *bytes = ws->bytes;
+  return Q8LIN_OK;
+}
+
+int q8lin_weight_bind_workspace(q8lin_weight* w, q8lin_workspace* ws) {
+  int st = validate_weight(w);
+  if (st != Q8LIN_OK) return st;
+  if (ws && ws->device != w->device)
+    return fail(Q8LIN_ERR_DEVICE, "workspace on device " + std::to_string(ws->device) + ", weight on device " +
+                                      std::to_string(w->device));
+  w->ws = ws;
+  return Q8LIN_OK;
+}
+
+int q8lin_set_wait_limit_ns(uint64_t ns) {
+  g_wait_limit_ns.store(ns, std::memory_order_relaxed);
+  return Q8LIN_OK;
+}
+
+uint64_t q8lin_wait_limit_ns(void) { return wait_limit_ns(); }
 
 int q8lin_dispatch_path(int64_t m, int64_t k, int64_t n) {
   if (m <= 0 || k <= 0 || n <= 0 || k % kQK) return -1;
@@ -387,17 +409,6 @@ int q8lin_dispatch_path(int64_t m, int64_t k, int64_t n) {
   if (use_gemv(m, k)) return (m == 1 && stream_applies(k)) ? Q8LIN_PATH_STREAM_GEMV : Q8LIN_PATH_GEMV;
   if (use_skinny(m)) return Q8LIN_PATH_INT8_TC;
   return Q8LIN_PATH_F16_TC;
-}
-
-int q8lin_reserve_workspace(int device, q8lin_stream_t stream, int64_t m, int64_t k) {
-  if (m < 0 || k <= 0 || k % kQK) return fail(Q8LIN_ERR_SHAPE, "reserve needs m >= 0 and k a positive multiple of 32");
-  int st = check_device(device);
-  if (st != Q8LIN_OK) return st;
-  const size_t need = workspace_bytes(m, k);
-  if (need == 0) return Q8LIN_OK;
-  DeviceGuard guard(device);
-  void* ws = nullptr;
-  return get_workspace(device, reinterpret_cast<cudaStream_t>(stream), need, &ws);
 }
 
 int q8lin_fault_status(int device, uint32_t* flags, int clear) {
@@ -526,10 +537,13 @@ size_t q8lin_allreduce_flag_bytes(int32_t world) {
 }
 
 int q8lin_forward_allreduce(const q8lin_weight* w, const float* x, float* y, int64_t m, void* const* stage_ptrs,
-                            void* const* flag_ptrs, int32_t rank, int32_t world, uint32_t epoch,
+                            void* const* flag_ptrs, int64_t stage_n, int32_t rank, int32_t world, uint32_t epoch,
                             const float* residual, q8lin_stream_t stream) {
   int st = validate_weight(w);
   if (st != Q8LIN_OK) return st;
+  if (world > 1 && w->n > stage_n)
+    return fail(Q8LIN_ERR_SHAPE, "the staging buffers hold " + std::to_string(stage_n) + " rows, the weight has " +
+                                     std::to_string(w->n));
   if (m != 1) return fail(Q8LIN_ERR_SHAPE, "the fused all-reduce takes one activation row (decode), got M=" + std::to_string(m));
   if (w->k > kFusedMaxK) return fail(Q8LIN_ERR_SHAPE, "the fused all-reduce needs K <= 8192");
   if (world < 1 || rank < 0 || rank >= world) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "rank must lie in [0, world)");

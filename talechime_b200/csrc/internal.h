@@ -8,6 +8,12 @@
 #include <atomic>
 #include <string>
 
+struct q8lin_workspace {
+  int device = -1;
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+
 struct q8lin_weight {
   int device = -1;
   int64_t n = 0;           // out features (rows)
@@ -15,9 +21,28 @@ struct q8lin_weight {
   int64_t row_stride = 0;  // bytes per repacked row
   uint8_t* packed = nullptr;
   size_t bytes = 0;
+  const q8lin_workspace* ws = nullptr;  // bound by q8lin_weight_bind_workspace; not owned
 };
 
 namespace q8lin {
+
+// Makes `device` current for the scope and restores the caller's device.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device);
+  ~DeviceGuard();
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+  bool ok() const { return ok_; }
+
+ private:
+  int prev_ = 0;
+  bool ok_ = false;
+  bool switched_ = false;
+};
+// Q8LIN_OK if `device` exists and is a compute-capability 10.0 GPU.
+int check_device(int device);
+bool aligned16(const void* p);
 
 // Error plumbing (thread-local message).
 int fail(int status, const std::string& msg);

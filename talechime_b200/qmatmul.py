@@ -28,6 +28,50 @@ def _stream_ptr(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+class Workspace:
+    """Device scratch of the batched paths (q8lin_workspace), sized for every M <= max_m
+    and K <= max_k.  ``Workspace.shared(device, m, k)`` is the one this process binds to
+    its weights on that device; growing it allocates (so ``QMatMul.reserve`` belongs before
+    a CUDA-graph capture), while ``q8lin_forward`` itself only reads it."""
+
+    _shared: dict = {}
+
+    def __init__(self, device: torch.device, max_m: int, max_k: int):
+        self.device = device
+        self.max_m = max_m
+        self.max_k = max_k
+        self._handle = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            check(_lib.lib().q8lin_workspace_create(device.index, max_m, max_k, ctypes.byref(self._handle)))
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._handle
+
+    def covers(self, m: int, k: int) -> bool:
+        return m <= self.max_m and k <= self.max_k
+
+    @classmethod
+    def shared(cls, device: torch.device, m: int, k: int) -> "Workspace":
+        cur = cls._shared.get(device.index)
+        if cur is None or not cur.covers(m, k):
+            if cur is not None:  # queued kernels may still read the old one
+                torch.cuda.synchronize(device)
+                m, k = max(m, cur.max_m), max(k, cur.max_k)
+            cur = cls(device, m, k)
+            cls._shared[device.index] = cur
+        return cur
+
+    def __del__(self):
+        h = getattr(self, "_handle", None)
+        if h is not None and h.value:
+            try:
+                _lib.lib().q8lin_workspace_destroy(h)
+            except Exception:
+                pass
+            self._handle = None
+
+
 class QMatMul:
     """One Q8_0 projection resident on one GPU (candle shape ``(n, k)`` = (out, in))."""
 
@@ -36,6 +80,17 @@ class QMatMul:
         self.n = n
         self.k = k
         self.device = device
+        self._ws: Optional[Workspace] = None
+
+    def reserve(self, max_m: int) -> None:
+        """Bind a workspace covering up to ``max_m`` activation rows (allocates when the
+        shared workspace of the device has to grow; q8lin_forward never does)."""
+        if _lib.lib().q8lin_workspace_bytes(max_m, self.k) == 0:
+            return
+        ws = Workspace.shared(self.device, max_m, self.k)
+        if ws is not self._ws:
+            check(_lib.lib().q8lin_weight_bind_workspace(self._handle, ws.handle))
+            self._ws = ws  # keeps it alive while bound
 
     # -- construction --------------------------------------------------------------
     @classmethod
@@ -132,6 +187,10 @@ class QMatMul:
             out = torch.empty(x.shape[:-1] + (self.n,), dtype=torch.float32, device=self.device)
         elif out.shape != x.shape[:-1] + (self.n,) or out.dtype != torch.float32 or not out.is_contiguous():
             raise Q8LinError(_lib.ERR_SHAPE, "out has the wrong shape, dtype or layout")
+        if m > 0 and _lib.lib().q8lin_workspace_size(self._handle, m) > 0 and (
+                self._ws is None or not self._ws.covers(m, self.k)
+                or self._ws is not Workspace._shared.get(self.device.index)):
+            self.reserve(m)
         check(_lib.lib().q8lin_forward(self._handle, ctypes.c_void_p(x.data_ptr()),
                                        ctypes.c_void_p(out.data_ptr()), m,
                                        ctypes.c_void_p(_stream_ptr(self.device))))

@@ -38,7 +38,7 @@ def test_library_exports_every_header_symbol(lib):
 
 
 def test_version(lib):
-    assert lib.q8lin_version() == 1
+    assert lib.q8lin_version() == 2
 
 
 def test_status_strings(lib):
@@ -110,3 +110,55 @@ def test_dispatch_follows_measured_crossovers(lib, m, k, n, path):
 def test_dispatch_rejects_invalid_sizes(lib):
     for m, k, n in ((0, 32, 1), (1, 33, 1), (1, 32, 0), (-1, 32, 1)):
         assert lib.q8lin_dispatch_path(m, k, n) == -1
+
+
+def test_wait_limit_round_trip():
+    """q8lin_set_wait_limit_ns: the time bound of the kernels' spin waits (default 1 s)."""
+    from talechime_b200 import _lib
+
+    L = _lib.lib()
+    old = L.q8lin_wait_limit_ns()
+    assert old == 1_000_000_000
+    try:
+        assert L.q8lin_set_wait_limit_ns(2_000_000) == 0
+        assert L.q8lin_wait_limit_ns() == 2_000_000
+    finally:
+        L.q8lin_set_wait_limit_ns(old)
+
+
+def test_workspace_sizes_cover_every_m():
+    """q8lin_workspace_bytes(max_m, max_k) covers what every M <= max_m, K <= max_k needs."""
+    from talechime_b200 import _lib
+
+    L = _lib.lib()
+    assert L.q8lin_workspace_bytes(0, 2048) == 0 and L.q8lin_workspace_bytes(8, 33) == 0
+    for max_m in (1, 4, 17, 32, 33, 256, 4096):
+        for max_k in (256, 2048, 6144):
+            total = L.q8lin_workspace_bytes(max_m, max_k)
+            for m in (1, 2, 5, 16, 17, 31, 32, 33, 64, 255, 256, 4095, 4096):
+                for k in (32, 256, 2048, 6144):
+                    if m <= max_m and k <= max_k:
+                        assert L.q8lin_workspace_bytes(m, k) <= total
+    h = ctypes.c_void_p()
+    assert L.q8lin_workspace_create(0, 0, 2048, ctypes.byref(h)) == _lib.ERR_SHAPE
+    assert L.q8lin_weight_bind_workspace(None, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.q8lin_workspace_destroy(None) == 0
+
+
+def _function_body(src, name):
+    i = src.index(f"int {name}(")
+    return src[i:src.index("\n}\n", i)]
+
+
+def test_forward_paths_do_not_allocate():
+    """The forward entry points and the kernel launchers they reach allocate no device
+    memory: no cudaMalloc / cudaFree of any flavour in their bodies."""
+    import os
+    import re
+
+    csrc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "talechime_b200", "csrc")
+    src = open(os.path.join(csrc, "abi.cu")).read()
+    for fn in ("q8lin_forward", "q8lin_forward_ws", "q8lin_forward_fused", "q8lin_forward_allreduce"):
+        assert not re.search(r"cuda(Malloc|Free)", _function_body(src, fn)), fn
+    for f in ("gemv.cu", "gemv_mrow.cu", "gemm_tc.cu", "gemm_skinny.cu", "mlp.cu", "layout.cu"):
+        assert not re.search(r"cuda(Malloc|Free)", open(os.path.join(csrc, f)).read()), f

@@ -157,3 +157,34 @@ def test_forward_ws_requires_workspace(cuda_device):
     assert st == 0
     torch.cuda.synchronize()
     assert torch.equal(y, q.forward(xd))
+
+
+def test_forward_needs_a_bound_workspace_and_allocates_nothing(oracle_lib, cuda_device):
+    """q8lin_forward reads scratch only from the workspace bound to the weight: without one
+    it returns Q8LIN_ERR_WORKSPACE; with one it runs inside a CUDA-graph capture in global
+    mode, where any device allocation would make the capture fail."""
+    import ctypes
+
+    from talechime_b200 import _lib
+
+    m, k, n = 40, 256, 72
+    x, w = synth.case(12, m, k, n)
+    q = QMatMul.from_gguf_blocks(w, n, k, device=cuda_device)
+    xd = torch.from_numpy(x).to(cuda_device)
+    y = torch.zeros((m, n), device=cuda_device)
+    L = _lib.lib()
+    s = torch.cuda.Stream(cuda_device)
+    args = (q.handle, ctypes.c_void_p(xd.data_ptr()), ctypes.c_void_p(y.data_ptr()), m, ctypes.c_void_p(s.cuda_stream))
+    assert L.q8lin_forward(*args) == _lib.ERR_WORKSPACE
+    assert b"q8lin_weight_bind_workspace" in L.q8lin_last_error()
+    q.reserve(64)
+    _lib.check(L.q8lin_forward(*args))  # eager warm-up (kernel attributes) before the capture
+    torch.cuda.synchronize()
+    y.zero_()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s, capture_error_mode="global"):
+        st = L.q8lin_forward(*args)
+    assert st == 0
+    g.replay()
+    torch.cuda.synchronize()
+    assert_close_to_oracle(y.cpu().numpy(), oracle_lib.matmul(x, w, n, threads=8))
