@@ -359,9 +359,12 @@ def run_prefill(torch, dist, L, dev, stream, mats, rank: int, world: int, m: int
 
 def run_tp_mlp(torch, dist, dev, rank: int, world: int, reps: int = 20) -> dict:
     """Config 4: the Q8_0 SwiGLU MLP at hidden 4096 / intermediate 14336 split over the
-    `world` ranks (gate/up by output rows, down by input blocks, one NCCL all-reduce per
-    forward; talechime_b200/tp_mlp.py).  Device time per forward with CUDA events, max
-    over ranks; every rank runs the same launches and collectives."""
+    `world` ranks through the C ABI (q8lin_mlp_tp_*: gate/up by output rows, down by input
+    blocks, ncclAllReduce on torch's communicator; for one row also the fused down
+    projection + NVLink sum).  Device time per forward with CUDA events on the launching
+    stream, max over ranks; every rank runs the same launches and collectives.  Every rank
+    also times the whole MLP on its own GPU (world 1), so each entry carries the speed-up
+    and the strong-scaling efficiency against one GPU."""
     from talechime_b200.tp_mlp import SwiGLUMLP
 
     hidden, inter = 4096, 14336
@@ -378,57 +381,59 @@ def run_tp_mlp(torch, dist, dev, rank: int, world: int, reps: int = 20) -> dict:
         return b
 
     gate, up, down = blocks(inter, hidden), blocks(inter, hidden), blocks(hidden, inter)
-    mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, rank=rank, world=world)
+    mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, rank=rank, world=world, max_m=256)
+    single = mlp if world == 1 else SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, max_m=256)
+    fused = (SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, rank=rank, world=world, max_m=1,
+                                        fused_decode=True) if world > 1 else None)
     del gate, up, down
     torch.cuda.synchronize(dev)
-    weight_bytes = 3 * inter * hidden * 34 // 32
-    out = {"config": f"SwiGLU MLP hidden {hidden} / intermediate {inter}, Q8_0, gate+up column-split, "
-                     f"down row-split over {world} GPU(s), NCCL all-reduce", "weight_bytes": weight_bytes,
-           "per_m": []}
-    for m in (1, 16, 256):
-        x = torch.randn((m, hidden), generator=gen, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def time_forward(m_obj, x, n):
         for _ in range(3):
-            mlp.forward(x)
+            m_obj.forward(x)
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        n = reps if m < 256 else max(3, reps // 2)
-        e0.record()
+        e0.record(stream)
         for _ in range(n):
-            mlp.forward(x)
-        e1.record()
+            m_obj.forward(x)
+        e1.record(stream)
         torch.cuda.synchronize(dev)
         ms = e0.elapsed_time(e1) / n
         if world > 1:
             t = torch.tensor([ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
-        out["per_m"].append({"m": m, "ms": ms, "weight_tb_s": weight_bytes / (ms * 1e-3) / 1e12,
-                             "tokens_per_s": m / (ms * 1e-3), "tflops": 2.0 * 3 * inter * hidden * m / (ms * 1e-3) / 1e12})
-    if world > 1:
-        # decode rows with the down projection and the cross-GPU sum in one kernel
-        mlp.enable_fused_allreduce()
+        return ms
+
+    weight_bytes = 3 * inter * hidden * 34 // 32
+    out = {"config": f"SwiGLU MLP hidden {hidden} / intermediate {inter}, Q8_0, gate+up column-split, "
+                     f"down row-split over {world} GPU(s), q8lin_mlp_tp_forward (ncclAllReduce)",
+           "weight_bytes": weight_bytes, "world": world, "per_m": []}
+    for m in (1, 16, 256):
+        x = torch.randn((m, hidden), generator=gen, device=dev)
+        n = reps if m < 256 else max(3, reps // 2)
+        ms = time_forward(mlp, x, n)
+        ms1 = ms if world == 1 else time_forward(single, x, n)
+        out["per_m"].append({"m": m, "ms": ms, "ms_1gpu": ms1, "speedup": ms1 / ms, "efficiency": ms1 / ms / world,
+                             "weight_tb_s": weight_bytes / (ms * 1e-3) / 1e12,
+                             "tokens_per_s": m / (ms * 1e-3),
+                             "tflops": 2.0 * 3 * inter * hidden * m / (ms * 1e-3) / 1e12})
+    if fused is not None:
         x = torch.randn((1, hidden), generator=gen, device=dev)
-        for _ in range(3):
-            mlp.forward(x)
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            mlp.forward(x)
-        e1.record()
-        torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / reps
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        out["m1_fused_allreduce"] = {"m": 1, "ms": ms, "weight_tb_s": weight_bytes / (ms * 1e-3) / 1e12,
-                                     "path": "gate_up GEMV, SwiGLU, down GEMV + cross-GPU sum in one kernel "
-                                             "(peer stores over NVLink, q8lin_forward_allreduce)"}
-        mlp.close_fused_allreduce()
-    del mlp
+        ms = time_forward(fused, x, reps)
+        ms1 = out["per_m"][0]["ms_1gpu"]
+        out["m1_fused_allreduce"] = {"m": 1, "ms": ms, "speedup": ms1 / ms, "efficiency": ms1 / ms / world,
+                                     "weight_tb_s": weight_bytes / (ms * 1e-3) / 1e12,
+                                     "path": "gate_up GEMV, then the down GEMV with SwiGLU in its activation "
+                                             "quantization and the cross-GPU sum in its tail (peer stores over "
+                                             "NVLink), Q8LIN_TP_FUSED_DECODE"}
+        fused.close()
+    if single is not mlp:
+        single.close()
+    mlp.close()
     torch.cuda.synchronize(dev)
     return out
 

@@ -287,6 +287,55 @@ int q8lin_forward_allreduce(const q8lin_weight* w, const float* x, float* y, int
                             const float* residual, q8lin_stream_t stream);
 
 /*
+ * Tensor-parallel Q8_0 SwiGLU MLP over `world` GPUs of one node: the VoxCPM MLP
+ * down(silu(gate(h)) * up(h)) (crates/voxcpm/src/transformer.rs:147-150, three
+ * Linear::forward calls, weights.rs:213-229) split with one exchange step -- gate and up
+ * by output rows (rank r keeps rows [I*r/P, I*(r+1)/P) of each, fused as one [gate; up]
+ * weight), SwiGLU local, down by Q8_0 block columns (I/P a multiple of 32), the partial
+ * outputs summed with ncclAllReduce on the caller's communicator.
+ * q8lin_mlp_tp_create: gate, up are the FULL [inter][hidden] Q8_0 GGUF tensors and down
+ *   the full [hidden][inter] one (host or device memory); the rank keeps its shards.
+ *   nccl_comm: an ncclComm_t of `world` ranks in which this process is `rank` (checked with
+ *   ncclCommCount / ncclCommUserRank; may be NULL when world == 1); NCCL is the
+ *   libnccl.so.2 the process has loaded (the one that made the communicator).  All scratch
+ *   for up to max_m activation rows is allocated here.
+ *   Q8LIN_TP_FUSED_DECODE (world > 1, hidden and inter/world <= 8192): create also
+ *   allocates staging and flag buffers; the caller gathers every rank's
+ *   q8lin_mlp_tp_peer_handle (Q8LIN_TP_HANDLE_BYTES each, in rank order) over its own
+ *   transport and passes them to q8lin_mlp_tp_connect_peers on every rank (IPC mappings:
+ *   the ranks share one node).  From then on one activation row runs the down projection
+ *   and the cross-GPU sum as one kernel per rank over NVLink peer memory (see
+ *   q8lin_forward_allreduce); before, M = 1 takes the NCCL path.
+ * q8lin_mlp_tp_forward: y[M][hidden] = the whole MLP of x[M][hidden] (x replicated on
+ *   every rank, y too).  Every rank calls it with the same M in the same order.  Allocates
+ *   nothing.  Q8LIN_ERR_NCCL when the all-reduce fails; on the fused path a rank that never
+ *   arrives makes the others time out (fault word bit 1, their output rows NaN).
+ * Teardown with the fused path: every rank calls q8lin_mlp_tp_close_peers (it waits for
+ *   its own work and unmaps the peers' buffers), the ranks meet at a host barrier, then
+ *   each calls q8lin_mlp_tp_destroy -- so no rank frees a buffer a peer still maps.  No
+ *   entry point here runs a collective except forward's all-reduce, so a rank that never
+ *   arrives cannot hang the others in create or teardown.
+ * q8lin_mlp_tp_shard: the shard plan alone (host only, no GPU): rows [row0, row0 + rows)
+ *   of gate and up, block columns [blk0, blk0 + blks) of down.
+ */
+typedef struct q8lin_mlp_tp q8lin_mlp_tp;
+#define Q8LIN_TP_FUSED_DECODE 1u
+#define Q8LIN_TP_HANDLE_BYTES (2 * Q8LIN_IPC_HANDLE_BYTES)
+int q8lin_mlp_tp_create(const void* gate_blocks, const void* up_blocks, const void* down_blocks, int64_t hidden,
+                        int64_t inter, int32_t rank, int32_t world, void* nccl_comm, int device, int64_t max_m,
+                        uint32_t flags, q8lin_stream_t stream, q8lin_mlp_tp** out);
+int q8lin_mlp_tp_peer_handle(const q8lin_mlp_tp* mlp, void* out);
+int q8lin_mlp_tp_connect_peers(q8lin_mlp_tp* mlp, const void* all_handles);
+int q8lin_mlp_tp_forward(q8lin_mlp_tp* mlp, const float* x, float* y, int64_t m, q8lin_stream_t stream);
+int q8lin_mlp_tp_close_peers(q8lin_mlp_tp* mlp);
+int q8lin_mlp_tp_destroy(q8lin_mlp_tp* mlp);
+int q8lin_mlp_tp_info(const q8lin_mlp_tp* mlp, int64_t* inter_local, int32_t* fused);
+int q8lin_mlp_tp_shard(int64_t hidden, int64_t inter, int32_t rank, int32_t world, int64_t* row0, int64_t* rows,
+                       int64_t* blk0, int64_t* blks);
+/* 1 if libnccl.so.2 could be resolved (already loaded, or loadable), else 0. */
+int q8lin_nccl_available(void);
+
+/*
  * Persistent decode step: a program of operations run by ONE cooperative launch (one
  * CTA per SM).  The weights of every GEMV stream through each SM's shared-memory ring
  * ahead of the data; operation i starts when every CTA has finished operation i - 1.

@@ -102,6 +102,17 @@ SIGNATURES = {
     "q8lin_allreduce_flag_bytes": (ctypes.c_size_t, [ctypes.c_int32]),
     "q8lin_forward_allreduce": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, _i64, ctypes.c_int32,
                                                 ctypes.c_int32, ctypes.c_uint32, _c_p, _c_p]),
+    "q8lin_mlp_tp_create": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _i64, ctypes.c_int32, ctypes.c_int32, _c_p,
+                                           ctypes.c_int, _i64, ctypes.c_uint32, _c_p, ctypes.POINTER(_c_p)]),
+    "q8lin_mlp_tp_peer_handle": (ctypes.c_int, [_c_p, _c_p]),
+    "q8lin_mlp_tp_connect_peers": (ctypes.c_int, [_c_p, _c_p]),
+    "q8lin_mlp_tp_forward": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _c_p]),
+    "q8lin_mlp_tp_close_peers": (ctypes.c_int, [_c_p]),
+    "q8lin_mlp_tp_destroy": (ctypes.c_int, [_c_p]),
+    "q8lin_mlp_tp_info": (ctypes.c_int, [_c_p, ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_int32)]),
+    "q8lin_mlp_tp_shard": (ctypes.c_int, [_i64, _i64, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(_i64),
+                                          ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
+    "q8lin_nccl_available": (ctypes.c_int, []),
     "q8lin_step_create": (ctypes.c_int, [ctypes.POINTER(Op), ctypes.c_int32, _c_p, _c_p, ctypes.c_int,
                                          ctypes.POINTER(_c_p)]),
     "q8lin_step_run": (ctypes.c_int, [_c_p, _c_p]),

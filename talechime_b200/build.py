@@ -20,7 +20,7 @@ LIB = os.path.join(PKG, "libq8lin.so")
 OBJDIR = os.path.join(PKG, "_build")
 
 SOURCES = ["abi.cu", "layout.cu", "gemv.cu", "gemm_simt.cu", "gemm_tc.cu", "noalloc.cu", "mlp.cu", "gemm_skinny.cu", "decoder.cu",
-           "step.cu", "gemv_mrow.cu", "gguf.cpp"]
+           "step.cu", "gemv_mrow.cu", "gguf.cpp", "tp_mlp.cu"]
 HEADERS = ["common.cuh", "internal.h"]
 
 NVCC_FLAGS = [
@@ -62,7 +62,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
             subprocess.run(cmd, check=True)
     if force or _stale(LIB, objs):
         cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-cudart", "static",
-               "-o", LIB, *objs]
+               "-o", LIB, *objs, "-ldl"]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)

@@ -1,6 +1,9 @@
-"""Tensor-parallel MLP host logic on the CPU: shard arithmetic, the SwiGLU oracle, and a
-world-size-2 gloo run of the partition (each rank's partial from the oracle, summed by
-all_reduce) against the unsplit oracle MLP."""
+"""Tensor-parallel MLP host logic on the CPU: the C-ABI shard plan (q8lin_mlp_tp_shard)
+and the argument checks of q8lin_mlp_tp_create that need no GPU, the SwiGLU oracle, and a
+world-size-2 gloo run of the partition -- each rank slices its shards by the C plan,
+computes its partial with the oracle, and gloo's all_reduce stands in for NCCL's --
+against the unsplit oracle MLP."""
+import ctypes
 import os
 import socket
 from datetime import timedelta
@@ -10,8 +13,9 @@ import pytest
 import torch
 
 from talechime_b200 import synth
+from talechime_b200 import _lib
 from talechime_b200._lib import Q8LinError
-from talechime_b200.tp_mlp import fuse_rows, shard_k, shard_rows
+from talechime_b200.tp_mlp import fuse_rows, shard_k, shard_plan, shard_rows
 from tests.conftest import assert_close_to_oracle
 
 HIDDEN, INTER = 256, 512
@@ -39,6 +43,46 @@ def test_k_shards_reassemble_blockwise():
         parts = [shard_k(down, HIDDEN, INTER, r, world) for r in range(world)]
         assert all(p.shape == (HIDDEN, INTER // 32 // world, 34) for p in parts)
         assert np.array_equal(np.concatenate(parts, axis=1).reshape(-1), down.reshape(-1))
+
+
+def test_c_shard_plan_matches_the_partition():
+    for world in (1, 2, 4, 8):
+        for r in range(world):
+            row0, rows, blk0, blks = shard_plan(4096, 14336, r, world)
+            assert (row0, rows) == (14336 // world * r, 14336 // world)
+            assert (blk0, blks) == (448 // world * r, 448 // world)
+
+
+def test_c_shard_plan_rejects_bad_splits():
+    L = _lib.lib()
+    out = [ctypes.c_int64() for _ in range(4)]
+    refs = [ctypes.byref(v) for v in out]
+    assert L.q8lin_mlp_tp_shard(4096, 14336, 0, 3, *refs) == _lib.ERR_SHAPE  # 448 blocks over 3
+    assert L.q8lin_mlp_tp_shard(4096, 14336, 2, 2, *refs) == _lib.ERR_INVALID_ARGUMENT
+    assert L.q8lin_mlp_tp_shard(4096, 14336 + 16, 0, 1, *refs) == _lib.ERR_SHAPE
+    assert L.q8lin_mlp_tp_shard(4096, 14336, 0, 1, None, None, None, None) == _lib.ERR_INVALID_ARGUMENT
+
+
+def test_c_create_checks_arguments_before_the_gpu():
+    """Errors the C entry point reports without touching CUDA (no GPU here)."""
+    L = _lib.lib()
+    h = ctypes.c_void_p()
+    buf = (ctypes.c_uint8 * 64)()
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    assert L.q8lin_mlp_tp_create(p, p, p, 256, 512, 0, 2, None, 0, 8, 0, None, ctypes.byref(h)) == \
+        _lib.ERR_INVALID_ARGUMENT  # world > 1 without a communicator
+    assert b"communicator" in L.q8lin_last_error()
+    assert L.q8lin_mlp_tp_create(None, p, p, 256, 512, 0, 1, None, 0, 8, 0, None, ctypes.byref(h)) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert L.q8lin_mlp_tp_create(p, p, p, 256, 512 + 32, 0, 2, None, 0, 8, 0, None, ctypes.byref(h)) == \
+        _lib.ERR_SHAPE  # 17 blocks over 2 ranks
+    assert L.q8lin_mlp_tp_create(p, p, p, 256, 512, 0, 1, None, 0, 0, 0, None, ctypes.byref(h)) == _lib.ERR_SHAPE
+    assert L.q8lin_mlp_tp_create(p, p, p, 256, 512, 0, 1, None, 0, 8, 8, None, ctypes.byref(h)) == \
+        _lib.ERR_INVALID_ARGUMENT  # unknown flag
+    assert L.q8lin_mlp_tp_forward(None, None, None, 1, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.q8lin_mlp_tp_peer_handle(None, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.q8lin_mlp_tp_destroy(None) == 0
+    assert L.q8lin_nccl_available() in (0, 1)
 
 
 def test_uneven_splits_are_rejected():
@@ -99,10 +143,11 @@ def _gloo_rank(rank, world, port, result_dir):
                                          world_size=world, timeout=timedelta(seconds=60))
     try:
         x, gate, up, down = _mlp_weights(7)
-        il = INTER // world
-        gu = np.concatenate([oracle.matmul(x, shard_rows(gate, INTER, HIDDEN, rank, world), il),
-                             oracle.matmul(x, shard_rows(up, INTER, HIDDEN, rank, world), il)], axis=1)
-        part = oracle.matmul(oracle.swiglu(gu), shard_k(down, HIDDEN, INTER, rank, world), HIDDEN)
+        row0, il, blk0, blks = shard_plan(HIDDEN, INTER, rank, world)  # the C plan of q8lin_mlp_tp_create
+        dn = np.ascontiguousarray(down[:, blk0:blk0 + blks])
+        gu = np.concatenate([oracle.matmul(x, np.ascontiguousarray(gate[row0:row0 + il]), il),
+                             oracle.matmul(x, np.ascontiguousarray(up[row0:row0 + il]), il)], axis=1)
+        part = oracle.matmul(oracle.swiglu(gu), dn, HIDDEN)
         y = torch.from_numpy(part.copy())
         torch.distributed.all_reduce(y, op=torch.distributed.ReduceOp.SUM)
         np.save(os.path.join(result_dir, f"y{rank}.npy"), y.numpy())

@@ -1,4 +1,8 @@
-"""SwiGLU kernel and the (tensor-parallel) Q8_0 MLP on the GPU against the oracle."""
+"""SwiGLU kernel and the (tensor-parallel) Q8_0 MLP on the GPU against the oracle.
+
+Stage by stage through one rank's QMatMuls (MLPShard, the same kernels), and end to end
+through the C-ABI object (SwiGLUMLP over q8lin_mlp_tp_*): on one GPU, and over NCCL with
+the sum done by ncclAllReduce or inside the down projection's kernel (fused decode)."""
 import ctypes
 import os
 import socket
@@ -9,7 +13,7 @@ import pytest
 import torch
 
 from talechime_b200 import _lib, synth
-from talechime_b200.tp_mlp import SwiGLUMLP, shard_k, shard_rows, swiglu
+from talechime_b200.tp_mlp import MLPShard, SwiGLUMLP, shard_k, shard_rows, swiglu
 from tests.conftest import assert_close_to_oracle
 
 pytestmark = pytest.mark.gpu
@@ -78,12 +82,40 @@ def test_swiglu_rejects_bad_arguments(cuda_device):
 def test_mlp_single_gpu_matches_oracle(oracle_lib, cuda_device, m):
     hidden, inter = 512, 1024
     x, gate, up, down = _weights(200 + m, hidden, inter, m)
-    mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device)
-    part = _check_stages(oracle_lib, mlp, x, gate, up, down, hidden, inter)
-    y = mlp.forward(torch.from_numpy(x).to(cuda_device)).cpu().numpy()
-    assert np.array_equal(y, part)  # forward() is the three stages
+    shard = MLPShard.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device)
+    part = _check_stages(oracle_lib, shard, x, gate, up, down, hidden, inter)
     ref = oracle_lib.mlp(x, gate, up, down, hidden, inter, threads=16)
+    mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device, max_m=128)
+    y = mlp.forward(torch.from_numpy(x).to(cuda_device)).cpu().numpy()
+    if m > 1:
+        assert np.array_equal(y, part)  # the C-ABI MLP runs the same three stages
+    # (M = 1: silu(gate) * up is folded into the down projection's quantization)
     assert _rel_l2(y, ref) <= MLP_E2E_REL_L2
+    mlp.close()
+
+
+def test_mlp_decode_row_folds_swiglu(oracle_lib, cuda_device):
+    """One activation row: gate|up GEMV, then the down GEMV with silu(gate) * up computed
+    in its activation quantization -- the same values q8lin_swiglu feeds the unfused path."""
+    hidden, inter = 1024, 2048
+    x, gate, up, down = _weights(210, hidden, inter, 1)
+    shard = MLPShard.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device)
+    mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device, max_m=4)
+    xt = torch.from_numpy(x).to(cuda_device)
+    y = mlp.forward(xt).cpu().numpy()
+    h = swiglu(shard.gate_up.forward(xt), inter).cpu().numpy()
+    assert_close_to_oracle(y, oracle_lib.matmul(h, down, hidden, threads=16))
+    mlp.close()
+
+
+def test_mlp_rejects_rows_beyond_max_m(cuda_device):
+    hidden, inter = 256, 512
+    x, gate, up, down = _weights(220, hidden, inter, 9)
+    mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device, max_m=8)
+    with pytest.raises(_lib.Q8LinError) as e:
+        mlp.forward(torch.from_numpy(x).to(cuda_device))
+    assert e.value.status == _lib.ERR_SHAPE
+    mlp.close()
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
@@ -95,7 +127,7 @@ def test_tp_partials_sum_to_oracle(oracle_lib, cuda_device, world):
     total_ref = np.zeros((m, hidden), dtype=np.float64)
     xt = torch.from_numpy(x).to(cuda_device)
     for r in range(world):
-        part = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device, rank=r, world=world)
+        part = MLPShard.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device, rank=r, world=world)
         p = _check_stages(oracle_lib, part, x, gate, up, down, hidden, inter, rank=r, world=world)
         assert np.array_equal(part.partial(xt).cpu().numpy(), p)
         total += p
@@ -106,12 +138,16 @@ def test_tp_partials_sum_to_oracle(oracle_lib, cuda_device, world):
     assert _rel_l2(total, ref) <= MLP_E2E_REL_L2
 
 
-def test_tp_forward_without_process_group_fails_loudly(cuda_device):
+def test_tp_create_without_process_group_fails_loudly(cuda_device):
     hidden, inter = 256, 512
-    x, gate, up, down = _weights(400, hidden, inter, 1)
-    part = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device, rank=0, world=2)
+    _, gate, up, down = _weights(400, hidden, inter, 1)
     with pytest.raises(_lib.Q8LinError):
-        part.forward(torch.from_numpy(x).to(cuda_device))
+        SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=cuda_device, rank=0, world=2)
+    L = _lib.lib()
+    h = ctypes.c_void_p()
+    ptrs = [ctypes.c_void_p(b.ctypes.data) for b in (gate, up, down)]
+    st = L.q8lin_mlp_tp_create(*ptrs, hidden, inter, 0, 2, None, 0, 4, 0, None, ctypes.byref(h))
+    assert st == _lib.ERR_INVALID_ARGUMENT and b"communicator" in L.q8lin_last_error()
 
 
 def _free_port():
@@ -126,28 +162,38 @@ def _nccl_rank(rank, world, port, result_dir):
                                          world_size=world, timeout=timedelta(seconds=60),
                                          device_id=torch.device("cuda", rank))
     try:
-        hidden, inter, m = 1024, 2048, 3
-        x, gate, up, down = _weights(500, hidden, inter, m)
+        hidden, inter = 1024, 2048
+        _, gate, up, down = _weights(500, hidden, inter, 1)
         dev = torch.device("cuda", rank)
-        mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, rank=rank, world=world)
-        y = mlp.forward(torch.from_numpy(x).to(dev))
+        mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, rank=rank, world=world,
+                                         max_m=64)
+        out = {}
+        for m in (1, 3, 40):
+            x = np.random.default_rng(510 + m).standard_normal((m, hidden)).astype(np.float32)
+            out[f"x{m}"] = x
+            out[f"y{m}"] = mlp.forward(torch.from_numpy(x).to(dev)).cpu().numpy()
         torch.cuda.synchronize(dev)
-        np.save(os.path.join(result_dir, f"y{rank}.npy"), y.cpu().numpy())
+        mlp.close()
+        np.savez(os.path.join(result_dir, f"y{rank}.npz"), **out)
     finally:
         torch.distributed.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp_nccl_two_gpus(oracle_lib, cuda_device, tmp_path):
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_nccl_multi_gpu(oracle_lib, cuda_device, tmp_path, world):
+    """The C-ABI MLP over `world` GPUs (ncclAllReduce on torch's communicator)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     port = _free_port()
     torch.multiprocessing.start_processes(_nccl_rank, args=(world, port, str(tmp_path)), nprocs=world,
                                           join=True, start_method="spawn")
-    x, gate, up, down = _weights(500, 1024, 2048, 3)
-    ref = oracle_lib.mlp(x, gate, up, down, 1024, 2048, threads=16)
-    y0, y1 = np.load(tmp_path / "y0.npy"), np.load(tmp_path / "y1.npy")
-    assert np.array_equal(y0, y1)
-    assert _rel_l2(y0, ref) <= MLP_E2E_REL_L2
+    _, gate, up, down = _weights(500, 1024, 2048, 1)
+    res = [np.load(tmp_path / f"y{r}.npz") for r in range(world)]
+    for m in (1, 3, 40):
+        ref = oracle_lib.mlp(res[0][f"x{m}"], gate, up, down, 1024, 2048, threads=16)
+        for r in range(world):
+            assert np.array_equal(res[r][f"y{m}"], res[0][f"y{m}"])  # every rank holds the same sum
+        assert _rel_l2(res[0][f"y{m}"], ref) <= MLP_E2E_REL_L2
 
 
 def _fused_rank(rank, world, port, result_dir):
@@ -159,22 +205,24 @@ def _fused_rank(rank, world, port, result_dir):
         hidden, inter = 1024, 2048
         dev = torch.device("cuda", rank)
         _, gate, up, down = _weights(600, hidden, inter, 1)
-        mlp = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, rank=rank, world=world)
-        mlp.enable_fused_allreduce()
-        xs, fused, nccl = [], [], []
+        fused = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, rank=rank, world=world,
+                                           max_m=4, fused_decode=True)
+        plain = SwiGLUMLP.from_gguf_blocks(gate, up, down, hidden, inter, device=dev, rank=rank, world=world,
+                                           max_m=4)
+        assert fused.fused_decode and not plain.fused_decode
+        xs, yf, yn = [], [], []
         for i in range(6):  # several calls: epochs and both staging halves
             x = np.random.default_rng(700 + i).standard_normal((1, hidden)).astype(np.float32)
             xd = torch.from_numpy(x).to(dev)
-            fused.append(mlp.forward(xd).cpu().numpy())
-            y = mlp.partial(xd)
-            torch.distributed.all_reduce(y)
-            nccl.append(y.cpu().numpy())
+            yf.append(fused.forward(xd).cpu().numpy())
+            yn.append(plain.forward(xd).cpu().numpy())
             xs.append(x)
         st = ctypes.c_uint32(0)
         _lib.check(_lib.lib().q8lin_fault_status(rank, ctypes.byref(st), 1))
-        mlp.close_fused_allreduce()
-        np.savez(os.path.join(result_dir, f"f{rank}.npz"), x=np.concatenate(xs), fused=np.concatenate(fused),
-                 nccl=np.concatenate(nccl), fault=np.array([st.value]))
+        fused.close()
+        plain.close()
+        np.savez(os.path.join(result_dir, f"f{rank}.npz"), x=np.concatenate(xs), fused=np.concatenate(yf),
+                 nccl=np.concatenate(yn), fault=np.array([st.value]))
     finally:
         torch.distributed.destroy_process_group()
 
@@ -182,7 +230,7 @@ def _fused_rank(rank, world, port, result_dir):
 @pytest.mark.parametrize("world", [2, 4])
 def test_fused_gemv_allreduce_matches_nccl(oracle_lib, cuda_device, tmp_path, world):
     """The down projection with the cross-GPU sum in the same kernel (peer stores over
-    NVLink) against the partial GEMV + NCCL all-reduce: bit-identical for two ranks (a
+    NVLink) against the down projection + ncclAllReduce: bit-identical for two ranks (a
     two-term sum does not depend on the order), within f32 tolerance otherwise."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
