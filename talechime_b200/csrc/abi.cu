@@ -6,6 +6,7 @@
 #include <stdlib.h>
 
 #include <atomic>
+#include <mutex>
 #include <string>
 #include <utility>
 #include <vector>
@@ -137,6 +138,21 @@ int check_device(int device) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+namespace {
+std::mutex g_attr_mu;
+}  // namespace
+
+cudaError_t ensure_smem(const void* fn, int* configured, int device, size_t smem, bool max_carveout) {
+  const int dev = (device >= 0 && device < 128) ? device : 0;
+  std::lock_guard<std::mutex> lock(g_attr_mu);
+  if ((int)smem <= configured[dev]) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess && max_carveout)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess) configured[dev] = (int)smem;
+  return e;
+}
 
 }  // namespace q8lin
 

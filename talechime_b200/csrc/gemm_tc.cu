@@ -240,7 +240,7 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
-      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.full[i], 3);  // the three copies of a stage, each from its own lane
       mbar_init(&sm.consumed[i], 1);
     }
     for (int i = 0; i < kBSlots; ++i) mbar_init(&sm.bfull[i], kConvWarps);
@@ -275,21 +275,34 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      pdl_wait();  // activations come from the upstream quantize kernel
-      int issued = 0;
-      for (int s = 0; s < nstages; ++s) {
-        const int st = s % kStages;
-        if (s >= kStages && !mbar_wait(&sm.consumed[st], ((s / kStages) - 1) & 1, abort)) break;
-        const int gs = sbeg + s;
-        mbar_expect_tx(&sm.full[st], kAStageBytes + kB8StageBytes + kDxStageBytes);
+    // Measured on B200: the TMA copies one thread issues complete one after another
+    // (~0.4 us each up to 16 KB, however many are in flight), while copies from different
+    // threads -- lanes of one warp included -- proceed side by side.  So the three copies
+    // of a stage (A, int8 B, activation scales) come from three lanes, rotating over
+    // kIssueTriples lane triples: each lane issues one copy every fourth stage.
+    constexpr int kIssueTriples = 4;
+    pdl_wait();  // activations come from the upstream quantize kernel
+    int issued = 0;
+    for (int s = 0; s < nstages; ++s) {
+      const int st = s % kStages;
+      if (s >= kStages && !warp_wait(&sm.consumed[st], ((s / kStages) - 1) & 1, abort)) break;
+      const int gs = sbeg + s;
+      const int l0 = 3 * (s % kIssueTriples);
+      if (lane == l0) {
+        mbar_expect_tx(&sm.full[st], kAStageBytes);
         tma_load_2d(sm.a[st], &map_a, gs * kBK, m0, &sm.full[st]);
+      } else if (lane == l0 + 1) {
+        mbar_expect_tx(&sm.full[st], kB8StageBytes);
         tma_load_2d(sm.b8[st], &map_b, gs * kBK, n0, &sm.full[st]);
+      } else if (lane == l0 + 2) {
+        mbar_expect_tx(&sm.full[st], kDxStageBytes);
         tma_load_2d(sm.dx[st], &map_dx, m0, 2 * gs, &sm.full[st]);
-        issued = s + 1;
       }
-      // Every copy this CTA issued must land before it can exit (on the normal path
-      // these waits return at once; after an abort they drain the copies).
+      issued = s + 1;
+    }
+    // Every copy this CTA issued must land before it can exit (on the normal path these
+    // waits return at once; after an abort they drain the copies).
+    if (lane == 0) {
       volatile int no_abort = 0;
       for (int s = (issued > kStages ? issued - kStages : 0); s < issued; ++s)
         mbar_wait(&sm.full[s % kStages], (s / kStages) & 1, &no_abort);

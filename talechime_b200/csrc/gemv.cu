@@ -475,22 +475,6 @@ size_t stream_smem_bytes(const StreamGeo& g, int64_t k) {
   return (size_t)g.nw * g.depth * g.slot_bytes + round16(k) + round16(4 * (k / kQK));
 }
 
-std::mutex g_attr_mu;
-
-// Opt-in of the dynamic shared memory a kernel needs, once per (device, size); with
-// max_carveout the carveout is set to the maximum so that two CTAs of the streaming
-// kernel fit an SM.
-cudaError_t ensure_smem(const void* fn, int* configured, int device, size_t smem, bool max_carveout) {
-  const int dev = (device >= 0 && device < 128) ? device : 0;
-  std::lock_guard<std::mutex> lock(g_attr_mu);
-  if ((int)smem <= configured[dev]) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e == cudaSuccess && max_carveout)
-    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-  if (e == cudaSuccess) configured[dev] = (int)smem;
-  return e;
-}
-
 template <bool kAllreduce, bool kXReg>
 cudaError_t launch_stream_t(const q8lin_weight& w, const float* x, float* y, const StreamGeo& g, cudaStream_t s,
                             const GemvFusion& fz) {

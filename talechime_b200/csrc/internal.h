@@ -43,6 +43,10 @@ class DeviceGuard {
 // Q8LIN_OK if `device` exists and is a compute-capability 10.0 GPU.
 int check_device(int device);
 bool aligned16(const void* p);
+// Opt-in of the dynamic shared memory of kernel `fn`, once per (device, size); `configured`
+// is the caller's per-device record (128 entries).  With max_carveout the carveout is set
+// to the maximum (two CTAs of the streaming GEMV share an SM).  Thread-safe.
+cudaError_t ensure_smem(const void* fn, int* configured, int device, size_t smem, bool max_carveout);
 
 // Error plumbing (thread-local message).
 int fail(int status, const std::string& msg);
