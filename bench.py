@@ -690,32 +690,54 @@ def main() -> None:
         off += y.numel()
     yptr2 = [ctypes.c_void_p(v.data_ptr()) for v in ycat_views]
 
-    def e2e_step():
-        for k, v in xin.items():
-            xs[k].copy_(v, non_blocking=True)
+    def e2e_calls():
         for h, xp, yp in zip(handles, xptr, yptr2):
             st = fwd(h, xp, yp, 1, sptr)
             if st:
                 _lib.check(st)
+
+    # The step's public-API calls recorded once as a CUDA graph, as the reference's decode
+    # loop records its step (crates/voxcpm/src/cuda_graph/replay.rs:46-80), then replayed
+    # per step between the H2D copy of the step's inputs and the D2H copy of its outputs.
+    e2e_calls()
+    torch.cuda.synchronize()
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph, stream=stream):
+        e2e_calls()
+    torch.cuda.synchronize()
+
+    def e2e_step(graphed):
+        for k, v in xin.items():
+            xs[k].copy_(v, non_blocking=True)
+        if graphed:
+            e2e_graph.replay()
+        else:
+            e2e_calls()
         yhost.copy_(yall, non_blocking=True)
         stream.synchronize()
 
-    for _ in range(args.warmup):
-        e2e_step()
-    if world > 1:
-        dist.barrier()
-    e2e_steps = max(1, args.steps // 4)
-    torch.cuda.synchronize()
-    ev0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    def time_e2e(graphed):
+        for _ in range(args.warmup):
+            e2e_step(graphed)
+        if world > 1:
+            dist.barrier()
+        steps = max(1, args.steps // 4)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(steps):
+            e2e_step(graphed)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        t_ms = ev0.elapsed_time(ev1) / steps
+        if world > 1:
+            t = torch.tensor([t_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_ms = float(t.item())
+        return t_ms, steps
+
+    e2e_ms, e2e_steps = time_e2e(True)
+    eager_ms, _ = time_e2e(False)
+    del e2e_graph
     e2e_value = world * bytes_per_step / (e2e_ms * 1e-3) / 1e12
 
     peak, peak_kind = load_peaks()
@@ -734,7 +756,10 @@ def main() -> None:
                      "bytes_per_launch": bytes_per_step / launches_per_step},
         "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms, "steps": e2e_steps,
-                "path": "q8lin_forward (C ABI via ctypes) x112, pinned H2D of x, D2H of y, stream sync per step"},
+                "path": "pinned H2D of the step's x, the 112 q8lin_forward calls (C ABI via ctypes) recorded once "
+                        "as a CUDA graph and replayed, D2H of every y, stream sync per step",
+                "eager": {"value": world * bytes_per_step / (eager_ms * 1e-3) / 1e12, "ms_per_step": eager_ms,
+                          "path": "the same with the 112 q8lin_forward calls issued from the host every step"}},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
     }
