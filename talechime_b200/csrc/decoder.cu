@@ -210,7 +210,6 @@ attention_decode_kernel(const float* __restrict__ q, const float* __restrict__ k
 constexpr int kRaCluster = 8;
 constexpr int kRaChunk = 32;
 constexpr int kRaThreads = 256;
-constexpr uint32_t kRaSpin = 1u << 24;
 
 __device__ unsigned int g_attn_fault;
 
@@ -228,15 +227,12 @@ struct RaSmem {
   alignas(8) uint64_t full[2];
 };
 
+// This CTA's wait limit (the kernel's wait_ns argument, set by thread 0 at entry).
+__shared__ uint64_t s_ra_wait_ns;
+
+// Bounded wait for this CTA's own bulk copies (false once the limit has passed).
 __device__ __forceinline__ bool ra_wait(uint64_t* bar, uint32_t parity) {
-  const uint32_t a = (uint32_t)__cvta_generic_to_shared(bar);
-  for (uint32_t i = 0; i < kRaSpin; ++i) {
-    uint32_t done;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-                 : "=r"(done) : "r"(a), "r"(parity) : "memory");
-    if (done) return true;
-  }
-  return false;
+  return mb_wait_ns((uint32_t)__cvta_generic_to_shared(bar), parity, s_ra_wait_ns, nullptr);
 }
 
 __device__ __forceinline__ void cluster_sync() {
@@ -246,7 +242,7 @@ __device__ __forceinline__ void cluster_sync() {
 __global__ void __launch_bounds__(kRaThreads)
 rope_attention_kernel(const float* __restrict__ qkv, const int* __restrict__ pos_dev, const float* __restrict__ cos_t,
                       const float* __restrict__ sin_t, float* __restrict__ kc, float* __restrict__ vc, int Hq, int Hkv,
-                      int max_t, float scale, float* __restrict__ out, int pos_ready) {
+                      int max_t, float scale, float* __restrict__ out, int pos_ready, uint64_t wait_ns) {
   constexpr int D = 128, half = 64;
   extern __shared__ __align__(16) uint8_t ra_raw[];
   RaSmem& sm = *reinterpret_cast<RaSmem*>(ra_raw);
@@ -256,6 +252,7 @@ rope_attention_kernel(const float* __restrict__ qkv, const int* __restrict__ pos
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
   const int group = Hq / Hkv, hk = h / group;
   if (tid == 0) {
+    s_ra_wait_ns = wait_ns;
     for (int i = 0; i < 2; ++i)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(&sm.full[i])),
                    "r"(1) : "memory");
@@ -557,7 +554,7 @@ cudaError_t launch_rope_attention(const float* qkv, const int* pos, const float*
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   const float scale = (float)(1.0 / std::sqrt(128.0));
   return cudaLaunchKernelEx(&cfg, rope_attention_kernel, qkv, pos, cos_t, sin_t, kc, vc, hq, hkv, max_t, scale, out,
-                            pos_ready ? 1 : 0);
+                            pos_ready ? 1 : 0, wait_limit_ns());
 }
 
 cudaError_t read_attention_fault(unsigned int* flags, bool clear) {

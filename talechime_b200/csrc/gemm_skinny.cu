@@ -47,7 +47,6 @@ constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kMaxTbufs = 8;
 constexpr int kTargetCtas = 148;
-constexpr uint32_t kSpinLimit = 1u << 24;
 
 constexpr int kAStageBytes = kRows * kStageK;     // 16 KB
 constexpr int kBStageBytes = kMaxNp * kStageK;    //  8 KB at Np = 64
@@ -77,18 +76,32 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
-  const uint32_t a = su32(b);
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    uint32_t ok;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-                 : "=r"(ok) : "r"(a), "r"(parity) : "memory");
-    if (ok) return true;
-    if ((i & 1023) == 1023 && *abort) return false;
+// This CTA's wait limit (the kernel's wait_ns argument, set by thread 0 at entry).
+__shared__ uint64_t s_wait_ns;
+
+// Bounded wait for the phase with the given parity; false (and the fault flag) once the
+// limit has passed, or false at once when the CTA aborted.  The spin lives out of line so
+// that the many call sites keep their registers; the first poll is inline.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t a, uint32_t parity, volatile int* abort) {
+  const uint64_t t0 = global_ns(), lim = s_wait_ns;
+  for (uint32_t i = 1;; ++i) {
+    if (mb_try(a, parity)) return true;
+    if ((i & 15u) == 0u) {
+      if (*abort) return false;
+      if (global_ns() - t0 > lim) break;
+    }
   }
   *abort = 1;
   atomicOr(&g_skinny_fault, 4u);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
+  const uint32_t a = su32(b);
+  return mb_try(a, parity) || mbar_wait_slow(a, parity, abort);
+}
+// Wait for this CTA's own copies / MMAs before it exits: the fixed drain bound.
+__device__ __forceinline__ bool mbar_drain(uint64_t* b, uint32_t parity) {
+  return mb_wait_ns(su32(b), parity, kDrainLimitNs, nullptr);
 }
 __device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
   return __all_sync(0xffffffffu, mbar_wait(b, parity, abort));
@@ -144,6 +157,7 @@ struct Params {
   uint32_t idesc;
   float* y;
   float* part;       // [tile][split][Np][128] partial sums (splits > 1)
+  uint64_t wait_ns;  // limit of the bounded waits (q8lin_set_wait_limit_ns)
 };
 
 template <int NP>
@@ -162,6 +176,7 @@ gemm_q8_0_skinny_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_
   volatile int* abort = &sm.abort;
 
   if (threadIdx.x == 0) {
+    s_wait_ns = p.wait_ns;
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.full[i], 3);  // the three copies of a stage, each from its own lane
       mbar_init(&sm.consumed[i], 1 + kEpiWarps);
@@ -210,9 +225,8 @@ gemm_q8_0_skinny_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_
       issued = s + 1;
     }
     if (lane == 0) {
-      volatile int no_abort = 0;
       for (int s = (issued > kStages ? issued - kStages : 0); s < issued; ++s)
-        mbar_wait(&sm.full[s % kStages], (s / kStages) & 1, &no_abort);
+        mbar_drain(&sm.full[s % kStages], (s / kStages) & 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issue ----------------
@@ -234,8 +248,7 @@ gemm_q8_0_skinny_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_
       umma_commit(&sm.consumed[st]);
     }
     umma_commit(&sm.mma_done);
-    volatile int no_abort = 0;
-    warp_wait(&sm.mma_done, 0, &no_abort);
+    __all_sync(0xffffffffu, mbar_drain(&sm.mma_done, 0));
   } else {
     // ---------------- epilogue ----------------
     const int quad = warp & 3;
@@ -457,6 +470,7 @@ cudaError_t launch_gemm_skinny(const q8lin_weight& w, const float* x, void* work
   p.idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(Np >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
   p.y = y;
   p.part = part;
+  p.wait_ns = wait_limit_ns();
 
   CUtensorMap mw, mx, md;
   if (!encode_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, K, N, (uint64_t)w.row_stride, kStageK, kRows,

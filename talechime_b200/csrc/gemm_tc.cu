@@ -65,7 +65,6 @@ constexpr int kEpiCols = kBN / (kEpiWarps / 4);  // TMEM columns per epilogue wa
 constexpr int kEpiWarp0 = 2 + kConvWarps;
 constexpr int kThreads = (kEpiWarp0 + kEpiWarps) * 32;
 constexpr uint32_t kTmemCols = 512;  // two blocks x (I: kBN columns + P: kBN columns)
-constexpr uint32_t kSpinLimit = 1u << 24;
 constexpr int kSplitMaxCtas = 148;  // tiles x splits bound when splitting (one wave)
 constexpr int kGroupStages = 4;     // stages per 8-block scale group: split boundaries
 
@@ -106,19 +105,32 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
 }
-// Bounded wait for the phase with the given parity; false (and the fault flag) on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
-  const uint32_t a = su32(b);
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    uint32_t ok;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-                 : "=r"(ok) : "r"(a), "r"(parity) : "memory");
-    if (ok) return true;
-    if ((i & 1023) == 1023 && *abort) return false;
+// This CTA's wait limit (the kernel's wait_ns argument, set by thread 0 at entry).
+__shared__ uint64_t s_wait_ns;
+
+// Bounded wait for the phase with the given parity; false (and the fault flag) once the
+// limit has passed, or false at once when the CTA aborted.  The spin lives out of line so
+// that the many call sites keep their registers; the first poll is inline.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t a, uint32_t parity, volatile int* abort) {
+  const uint64_t t0 = global_ns(), lim = s_wait_ns;
+  for (uint32_t i = 1;; ++i) {
+    if (mb_try(a, parity)) return true;
+    if ((i & 15u) == 0u) {
+      if (*abort) return false;
+      if (global_ns() - t0 > lim) break;
+    }
   }
   *abort = 1;
   atomicOr(&g_tc_fault, 1u);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
+  const uint32_t a = su32(b);
+  return mb_try(a, parity) || mbar_wait_slow(a, parity, abort);
+}
+// Wait for this CTA's own copies / MMAs before it exits: the fixed drain bound.
+__device__ __forceinline__ bool mbar_drain(uint64_t* b, uint32_t parity) {
+  return mb_wait_ns(su32(b), parity, kDrainLimitNs, nullptr);
 }
 // Every lane waits (and so acquires); the verdict is made warp-uniform.
 __device__ __forceinline__ bool warp_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
@@ -220,7 +232,7 @@ __device__ __forceinline__ uint2 i8x4_to_f16x4(uint32_t w) {
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                     const __grid_constant__ CUtensorMap map_dx, const uint8_t* __restrict__ W, int64_t S, int N,
-                    int K, float* __restrict__ y, int M, int splits, float* __restrict__ part) {
+                    int K, float* __restrict__ y, int M, int splits, float* __restrict__ part, uint64_t wait_ns) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
@@ -239,6 +251,7 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   volatile int* abort = &sm.abort;
 
   if (threadIdx.x == 0) {
+    s_wait_ns = wait_ns;
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&sm.full[i], 3);  // the three copies of a stage, each from its own lane
       mbar_init(&sm.consumed[i], 1);
@@ -303,9 +316,8 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     // Every copy this CTA issued must land before it can exit (on the normal path these
     // waits return at once; after an abort they drain the copies).
     if (lane == 0) {
-      volatile int no_abort = 0;
       for (int s = (issued > kStages ? issued - kStages : 0); s < issued; ++s)
-        mbar_wait(&sm.full[s % kStages], (s / kStages) & 1, &no_abort);
+        mbar_drain(&sm.full[s % kStages], (s / kStages) & 1);
     }
   } else if (warp == 1) {
     // ---------------- MMA issue ----------------
@@ -342,8 +354,7 @@ gemm_q8_0_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
     }
     // all MMAs this warp issued have completed before TMEM is released
     umma_commit(&sm.mma_done);
-    volatile int no_abort = 0;
-    warp_wait(&sm.mma_done, 0, &no_abort);
+    __all_sync(0xffffffffu, mbar_drain(&sm.mma_done, 0));
   } else if (warp < kEpiWarp0) {
     // ---------------- int8 -> f16 conversion, scale operands ----------------
     const int ct = threadIdx.x - 64;  // 0..127: also the weight row n0 + ct and activation row m0 + ct
@@ -652,7 +663,7 @@ cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspac
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_q8_0_tc_kernel, map_a, map_b, map_dx, (const uint8_t*)w.packed,
-                                     w.row_stride, N, K, y, M, splits, part);
+                                     w.row_stride, N, K, y, M, splits, part, wait_limit_ns());
   if (e != cudaSuccess || splits == 1) return e;
   // 3. split-K: add the partials
   const int tiles_n = (N + kBN - 1) / kBN;

@@ -17,9 +17,12 @@
 //     finished operation i - 1 (a per-operation arrival counter: release add by one
 //     thread of each CTA after a CTA barrier, acquire poll by one thread of the waiting
 //     CTA before a CTA barrier), the only synchronisation between CTAs;
-//   * a consumer warp waits only on the ring chunks that hold its rows; a per-slot
-//     tally of finished (row pair, segment) tasks in shared memory tells the warp that
-//     completes it to release the slot (empty barrier count 1).
+//   * every consumer warp consumes every ring chunk in order -- waits for it, does its
+//     pairs if it has any -- and arrives on the chunk's empty barrier, which counts all
+//     consumer warps: the producer is then never more than one ring ahead of any warp,
+//     so the parity a warp waits on always names the chunk it wants.  (Waiting only for
+//     the chunks holding its own rows let a warp test the next use of a slot whose
+//     current copy had not landed, where the parity test passes at once.)
 // GEMV work split: CTA c owns rows [N c / G, N (c + 1) / G) (with the SwiGLU epilogue:
 // pairs (gate i, up i) for i in [I c / G, I (c + 1) / G), the gate and up rows of a pair
 // copied into the same ring chunk).  A row's K values form ceil(K / 2048) segments;
@@ -33,6 +36,8 @@
 // Every wait is bounded: on timeout bit 4 of the fault word is set, the other CTAs
 // stop waiting soon after, and the kernel ends without hanging (outputs invalid).
 #include <cmath>
+
+#include <climits>
 
 #include "common.cuh"
 #include "internal.h"
@@ -51,8 +56,6 @@ constexpr int kSMaxRpc = 8;
 constexpr int kSMaxSegs = 4;
 constexpr int kSMaxResidualRows = kSConsumers;
 constexpr int kSplits = 8;                     // attention splits per q head
-constexpr uint32_t kSpin = 1u << 24;           // mbarrier polls
-constexpr uint32_t kCountSpin = 1u << 22;      // arrival-counter polls (with backoff)
 
 __device__ unsigned int g_step_fault;
 
@@ -71,7 +74,7 @@ struct SmemLayout {
   static constexpr int avc = akc + 128 * 4;                        // f32 [128] current v
   static constexpr int awp = avc + 128 * 4;                        // f32 [kSWarps][132] warp partials
   static constexpr int flag = awp + kSWarps * 132 * 4;             // int [4]
-  static constexpr int tally = flag + 16;                          // int [kSlots] tasks done per slot
+  static constexpr int tally = flag + 16;                          // int [kSlots] (spare)
   static constexpr int full = tally + (kSlots * 4 + 15) / 16 * 16;  // u64 [kSlots]
   static constexpr int empty = full + kSlots * 8;                  // u64 [kSlots]
   static constexpr int bytes = empty + kSlots * 8;
@@ -85,16 +88,28 @@ __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvt
 // After any wait of any CTA has timed out, the others stop waiting too (within ~1k polls).
 __device__ __forceinline__ bool step_aborted() { return (*(volatile unsigned*)&g_step_fault & 16u) != 0u; }
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpin; ++i) {
-    uint32_t ok;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-                 : "=r"(ok) : "r"(su32(bar)), "r"(parity) : "memory");
-    if (ok) return true;
-    if ((i & 1023u) == 1023u && step_aborted()) return false;
+// This CTA's wait limit (the kernel's wait_ns argument, set by thread 0 at entry).
+__shared__ uint64_t s_step_wait_ns;
+
+__device__ __noinline__ bool mbar_wait_slow(uint32_t a, uint32_t parity) {
+  const uint64_t t0 = global_ns(), lim = s_step_wait_ns;
+  for (uint32_t i = 1;; ++i) {
+    if (mb_try(a, parity)) return true;
+    if ((i & 15u) == 0u) {
+      if (step_aborted()) return false;
+      if (global_ns() - t0 > lim) break;
+    }
   }
   atomicOr(&g_step_fault, 16u);
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = su32(bar);
+  return mb_try(a, parity) || mbar_wait_slow(a, parity);
+}
+// Wait for this CTA's own bulk copies before it exits: the fixed drain bound.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+  return mb_wait_ns(su32(bar), parity, kDrainLimitNs, nullptr);
 }
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -107,12 +122,16 @@ __device__ __forceinline__ void red_release(unsigned* p) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(1u) : "memory");
 }
 
-// One thread waits until the counter reaches `target`.
+// One thread waits until the counter reaches `target` (bounded in time).
 __device__ __forceinline__ void wait_count(const unsigned* p, unsigned target) {
-  for (uint32_t i = 0; i < kCountSpin; ++i) {
+  const uint64_t t0 = global_ns(), lim = s_step_wait_ns;
+  for (uint32_t i = 0;; ++i) {
     if (ld_acquire(p) >= target) return;
     if (i > 256) __nanosleep(20);
-    if ((i & 1023u) == 1023u && step_aborted()) return;
+    if ((i & 15u) == 15u) {
+      if (step_aborted()) return;
+      if (global_ns() - t0 > lim) break;
+    }
   }
   atomicOr(&g_step_fault, 16u);
 }
@@ -210,9 +229,8 @@ __device__ void gemv_prologue(const StepOp& op, const float4 (&wn)[kQuadGroups],
 }
 
 // One GEMV operation on the consumer side.  `seq` is the ring position of its first
-// chunk.  A warp touches only the chunks in which it has pairs; each such warp adds its
-// pair count to the chunk's shared-memory tally and the warp that completes the tally
-// releases the slot (empty barrier count 1).
+// chunk.  Every consumer warp waits for every chunk in order and arrives once on its
+// empty barrier; warps beyond the op's groups (K = 8192) only wait and arrive.
 __device__ void gemv_consume(const StepOp& op, int c, int g, int seq, uint8_t* sm, float* am_v, int* am_i) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool swi = op.epilogue == kStepEpilogueSwiGLU;
@@ -222,11 +240,10 @@ __device__ void gemv_consume(const StepOp& op, int c, int g, int seq, uint8_t* s
   const int64_t S = op.S;
   const int nseg = (nb + 63) >> 6, ngroups = kSWarps / nseg;
   const int seg = warp % nseg, grp = warp / nseg;
-  if (grp >= ngroups) return;  // K = 6144 with 15 warps uses all; K = 8192: three idle warps
+  const bool idle = grp >= ngroups;  // K = 6144 with 15 warps uses all; K = 8192: three idle warps
   const int nchunks = (nunits_cta + cu - 1) / cu;
   float* part = reinterpret_cast<float*>(sm + SmemLayout::part);
   int* cnt = reinterpret_cast<int*>(sm + SmemLayout::cnt);
-  int* tally = reinterpret_cast<int*>(sm + SmemLayout::tally);
   const float* res = reinterpret_cast<const float*>(sm + SmemLayout::res);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + SmemLayout::full);
   uint64_t* empty = reinterpret_cast<uint64_t*>(sm + SmemLayout::empty);
@@ -247,14 +264,10 @@ __device__ void gemv_consume(const StepOp& op, int c, int g, int seq, uint8_t* s
       bi = grow;
     }
   };
-  int off = grp;  // this warp's first pair in the current chunk: pairs go round-robin over the groups
+  int off = idle ? INT_MAX / 2 : grp;  // this warp's first pair in the current chunk: pairs go round-robin
   for (int jj = 0; jj < nchunks; ++jj) {
     const int i0 = jj * cu, nu = min(cu, nunits_cta - i0);
     const int npairs = swi ? nu : (nu + 1) >> 1;
-    if (off >= npairs) {  // nothing for this warp here
-      off -= npairs;
-      continue;
-    }
     const int j = seq + jj, slot = j % kSlots;
     mbar_wait(&full[slot], (uint32_t)((j / kSlots) & 1));
     const uint8_t* chunk = sm + SmemLayout::ring + (size_t)slot * kSlotBytes;
@@ -294,18 +307,10 @@ __device__ void gemv_consume(const StepOp& op, int c, int g, int seq, uint8_t* s
         }
       }
     }
-    off = p - npairs;
+    if (!idle) off = p - npairs;
+    (void)done_pairs;
     __syncwarp();
-    if (lane == 0) {
-      // every (pair, segment) task of the chunk counts once; the warp completing the
-      // tally releases the slot
-      const int total = npairs * nseg;
-      __threadfence_block();
-      if (atomicAdd(&tally[slot], done_pairs) + done_pairs == total) {
-        tally[slot] = 0;
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&empty[slot])) : "memory");
-      }
-    }
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&empty[slot])) : "memory");
   }
   if (op.argmax && lane == 0) {
     am_v[warp] = bv;
@@ -495,23 +500,22 @@ __device__ void attention_unit(const StepOp& op, int unit, int pos, uint8_t* sm,
 
 __global__ void __launch_bounds__(kSThreads, 1)
 decode_step_kernel(const StepOp* __restrict__ ops, int nops, int* __restrict__ pos_dev, int* __restrict__ token,
-                   unsigned* __restrict__ done, float* __restrict__ am_gv, int* __restrict__ am_gi) {
+                   unsigned* __restrict__ done, float* __restrict__ am_gv, int* __restrict__ am_gi, uint64_t wait_ns) {
   extern __shared__ __align__(16) uint8_t sm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x, g = gridDim.x;
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + SmemLayout::full);
   uint64_t* empty = reinterpret_cast<uint64_t*>(sm + SmemLayout::empty);
   if (tid == 0) {
+    s_step_wait_ns = wait_ns;
     for (int i = 0; i < kSlots; ++i) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&full[i])), "r"(1) : "memory");
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&empty[i])), "r"(1) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(&empty[i])), "r"(kSWarps) : "memory");
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   int* cnt = reinterpret_cast<int*>(sm + SmemLayout::cnt);
   for (int i = tid; i < kSlots * kSMaxRpc; i += kSThreads) cnt[i] = 0;
-  int* tally = reinterpret_cast<int*>(sm + SmemLayout::tally);
-  for (int i = tid; i < kSlots; i += kSThreads) tally[i] = 0;
   __syncthreads();
 
   if (warp == kSWarps) {
@@ -547,7 +551,7 @@ decode_step_kernel(const StepOp* __restrict__ ops, int nops, int* __restrict__ p
         }
       }
       // the copies must land before the CTA's shared memory is released
-      for (int i = (j > kSlots ? j - kSlots : 0); i < j; ++i) mbar_wait(&full[i % kSlots], (uint32_t)((i / kSlots) & 1));
+      for (int i = (j > kSlots ? j - kSlots : 0); i < j; ++i) mbar_drain(&full[i % kSlots], (uint32_t)((i / kSlots) & 1));
     }
     return;
   }
@@ -713,7 +717,7 @@ cudaError_t launch_decode_step(const StepOp* ops, int nops, int* pos, int* token
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, decode_step_kernel, ops, nops, pos, token, done, am_gv, am_gi);
+  return cudaLaunchKernelEx(&cfg, decode_step_kernel, ops, nops, pos, token, done, am_gv, am_gi, wait_limit_ns());
 }
 
 cudaError_t step_max_grid(int device, int* grid) {

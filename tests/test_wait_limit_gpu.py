@@ -77,3 +77,4 @@ def test_staging_smaller_than_the_weight_is_rejected(cuda_device):
                                    ctypes.c_void_p(p.data_ptr()), ctypes.c_void_p(p.data_ptr()), n - 1, 0, 2, 1, None,
                                    None)
     assert st == _lib.ERR_SHAPE and b"staging" in L.q8lin_last_error()
+
