@@ -45,7 +45,7 @@ def test_skinny_without_split_is_bit_exact(oracle_lib, cuda_device):
 
 
 def test_skinny_repeated_calls_are_deterministic(cuda_device):
-    """Split-K partials are added by the last CTA of a tile in split order."""
+    """Split-K partials are added by a separate reduction kernel in split order."""
     x, w = synth.case(612, 8, 4096, 1024)
     q = QMatMul.from_gguf_blocks(w, 1024, 4096, device=cuda_device)
     xt = torch.from_numpy(x).to(cuda_device)

@@ -64,7 +64,7 @@ def test_tc_integer_products_are_exact(cuda_device, k):
 
 
 def test_tc_split_k_is_deterministic(cuda_device):
-    """The last CTA of a tile adds the split partials in split order."""
+    """Split-K partial tiles are added by a separate reduction kernel in split order."""
     x, w = synth.case(403, 64, 6144, 1024)
     q = QMatMul.from_gguf_blocks(w, 1024, 6144, device=cuda_device)
     xt = torch.from_numpy(x).to(cuda_device)
