@@ -85,6 +85,17 @@ __device__ __forceinline__ bool mb_wait_ns(uint32_t bar, uint32_t parity, uint64
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
+// Weights are read once per call: an L2 evict-first policy keeps the streamed rows from
+// pushing activations, outputs and caches out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void cp_async16_stream(uint32_t dst, const void* src, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "l"(policy)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 // All but the newest `n` (0..3) of this thread's copy groups have landed.
 __device__ __forceinline__ void cp_async_wait(int n) {
@@ -258,6 +269,121 @@ __device__ __forceinline__ void warp_sum2(float& ta, float& tb) {
     ta += __shfl_xor_sync(kFull, ta, o);
     tb += __shfl_xor_sync(kFull, tb, o);
   }
+}
+
+// Sum over the warp of v[m], m < MR, leaving in every lane the total of row mr_index(lane):
+// at each of the first log2(MR) levels a lane keeps half of its values and adds the
+// partner's copy of them, so MR rows cost MR - 1 + 5 - log2(MR) shuffles over 5 levels
+// (one shuffle tree per row would cost 5 MR).
+template <int MR>
+__device__ __forceinline__ float transpose_reduce(float (&v)[MR], int lane) {
+#pragma unroll
+  for (int L = 0; L < 5; ++L) {
+    const int o = 16 >> L;
+    const int c = MR >> L;  // values held before this level
+    if (c > 1) {
+      const bool up = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < MR / 2; ++i) {
+        if (i < c / 2) {
+          const float send = up ? v[i] : v[i + c / 2];
+          const float keep = up ? v[i + c / 2] : v[i];
+          v[i] = keep + __shfl_xor_sync(kFull, send, o);
+        }
+      }
+    } else {
+      v[0] += __shfl_xor_sync(kFull, v[0], o);
+    }
+  }
+  return v[0];
+}
+
+template <int MR>
+__device__ __forceinline__ int mr_index(int lane) {
+  int m = 0;
+#pragma unroll
+  for (int L = 0; L < 5; ++L) {
+    const int c = MR >> L;
+    if (c > 1 && (lane & (16 >> L))) m += c / 2;
+  }
+  return m;
+}
+
+// The same arithmetic on rows addressed by their 32-bit shared-memory address, with
+// explicit ld.shared loads (a row pointer built with run-time offsets from a dynamic
+// shared array otherwise compiles to generic loads).
+__device__ __forceinline__ int4 lds128(uint32_t a) {
+  int4 v;
+  asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float lds_half_f32(uint32_t a) {
+  unsigned short h;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
+  return __half2float(__ushort_as_half(h));
+}
+__device__ __forceinline__ float block_term_s(uint32_t row, int K, int blk, const int4& x0, const int4& x1, float dxs) {
+  const uint32_t h = (uint32_t)half_order(threadIdx.x & 31) * 16u;
+  const uint32_t b = row + (uint32_t)blk * 32u;
+  const int4 w0 = lds128(b + h);
+  const int4 w1 = lds128(b + (16u - h));
+  const int isum = dot16(w1, x1, dot16(w0, x0, 0));  // exact in int32 either way
+  const float dw = lds_half_f32(row + (uint32_t)K + 2u * (uint32_t)blk);
+  return __fmul_rn(__fmul_rn(__int2float_rn(isum), dw), dxs);
+}
+__device__ __forceinline__ float seg_terms1_s(uint32_t row, int K, int seg, const XSeg& xs) {
+  const int lane = threadIdx.x & 31;
+  const int b0 = seg * 64 + lane, b1 = b0 + 32;
+  float t = 0.0f;
+  if (xs.va) t = block_term_s(row, K, b0, xs.a0, xs.a1, xs.da);
+  if (xs.vb) t = __fadd_rn(t, block_term_s(row, K, b1, xs.b0, xs.b1, xs.db));
+  return t;
+}
+__device__ __forceinline__ void seg_terms2_s(uint32_t wa, uint32_t wb, bool has_b, int K, int seg, const XSeg& xs,
+                                             float& ta, float& tb) {
+  const int lane = threadIdx.x & 31;
+  const int b0 = seg * 64 + lane, b1 = b0 + 32;
+  ta = 0.0f;
+  tb = 0.0f;
+  if (xs.va) {
+    ta = block_term_s(wa, K, b0, xs.a0, xs.a1, xs.da);
+    if (has_b) tb = block_term_s(wb, K, b0, xs.a0, xs.a1, xs.da);
+  }
+  if (xs.vb) {
+    ta = __fadd_rn(ta, block_term_s(wa, K, b1, xs.b0, xs.b1, xs.db));
+    if (has_b) tb = __fadd_rn(tb, block_term_s(wb, K, b1, xs.b0, xs.b1, xs.db));
+  }
+}
+// load_xseg from the quantized activations at shared addresses qx (int8 [K]) and dx
+// (f32 [K/32]).
+__device__ __forceinline__ XSeg load_xseg_s(uint32_t qx, uint32_t dx, int nb, int seg) {
+  const int lane = threadIdx.x & 31, b0 = seg * 64 + lane, b1 = b0 + 32;
+  const uint32_t h = (uint32_t)half_order(lane) * 16u;
+  XSeg xs;
+  xs.va = b0 < nb;
+  xs.vb = b1 < nb;
+  const int4 z = make_int4(0, 0, 0, 0);
+  xs.a0 = xs.va ? lds128(qx + (uint32_t)b0 * 32u + h) : z;
+  xs.a1 = xs.va ? lds128(qx + (uint32_t)b0 * 32u + (16u - h)) : z;
+  xs.b0 = xs.vb ? lds128(qx + (uint32_t)b1 * 32u + h) : z;
+  xs.b1 = xs.vb ? lds128(qx + (uint32_t)b1 * 32u + (16u - h)) : z;
+  float da = 0.0f, db = 0.0f;
+  if (xs.va) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(da) : "r"(dx + 4u * (uint32_t)b0));
+  if (xs.vb) asm volatile("ld.shared.f32 %0, [%1];" : "=f"(db) : "r"(dx + 4u * (uint32_t)b1));
+  xs.da = da;
+  xs.db = db;
+  return xs;
+}
+
+// This lane's share of segment `seg` of one row: the sum of its two block terms (the
+// same value seg_terms2 gives for either of its rows).
+__device__ __forceinline__ float seg_terms1(const uint8_t* w, int K, int seg, const XSeg& xs) {
+  const int lane = threadIdx.x & 31;
+  const int b0 = seg * 64 + lane, b1 = b0 + 32;
+  float t = 0.0f;
+  if (xs.va) t = block_term(w, K, b0, xs.a0, xs.a1, xs.da);
+  if (xs.vb) t = __fadd_rn(t, block_term(w, K, b1, xs.b0, xs.b1, xs.db));
+  return t;
 }
 
 __device__ __forceinline__ void seg_dot2(const uint8_t* wa, const uint8_t* wb, bool has_b, int K, int seg,

@@ -26,6 +26,7 @@
 //      the warp.  The sum over blocks is a tree, so outputs agree with the
 //      sequential CPU order within f32 summation tolerance.
 // Nothing upstream (x) is read and nothing (y) is written before step 2.
+#include <type_traits>
 #include <stdio.h>
 #include <stdlib.h>
 
@@ -249,6 +250,7 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
 
   // the warp's t-th slot (CTA slot warp + t * nw) into ring position t % depth; one copy
   // group per slot, empty when the warp has no such slot
+  const uint64_t l2pol = l2_evict_first_policy();
   auto issue = [&](int t) {
     const int j = warp + t * nw;
     if (j < nslots) {
@@ -256,12 +258,31 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
       const int units = (min(rps, nrows - row) * (int)S) >> 4;
       const uint8_t* src = W + (size_t)(r0 + row) * S;
       const uint32_t dst = smem_u32(ring + (size_t)(t % depth) * geo.slot_bytes);
-      for (int u = lane; u < units; u += 32) cp_async16(dst + 16u * u, src + 16 * (size_t)u);
+      for (int u = lane; u < units; u += 32) cp_async16_stream(dst + 16u * u, src + 16 * (size_t)u, l2pol);
     }
     cp_async_commit();
   };
   if (warp < nw)
     for (int t = 0; t < depth; ++t) issue(t);
+
+  // Where the prefetched slots (the first `depth` of every ring) hold all of the CTA's
+  // rows ("all" mode), every warp takes a share of them once the activations are ready;
+  // their shared addresses are tabulated here, before the dependency wait.  Where more
+  // rows follow ("own" mode), each ring warp streams its own slots through its ring.
+  const int pre_slots = min(nslots, nw * depth);
+  const int p1_rows = min(nrows, pre_slots * rps);
+  const int p1_cap = nw * depth * rps;
+  const bool own = nslots > nw * depth;
+  const int nseg = (K + kSegValues - 1) / kSegValues;
+  float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(dx) + round16(4 * nb));  // [nseg][p1_rows]
+  uint32_t* rowaddr = reinterpret_cast<uint32_t*>(part + (nseg > 1 ? nseg * p1_cap : 0));
+  const uint32_t smem_s = smem_u32(smem);
+  if (!own) {
+    for (int rr = threadIdx.x; rr < p1_rows; rr += kStreamThreads) {
+      const int j = rr / rps;
+      rowaddr[rr] = smem_s + (uint32_t)(((j % nw) * depth + j / nw) * geo.slot_bytes + (rr - j * rps) * (int)S);
+    }
+  }
 
   // ---------------- x -> Q8_0 in shared memory (all 16 warps) ----------------
   {
@@ -341,64 +362,110 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
       }
     }
   }
+  // the slots issued before the dependency wait are complete for every warp after this
+  // barrier (they were issued long before; the wait only matters for a first launch)
+  if (warp < nw) cp_async_wait(0);
   __syncthreads();
-  if (warp >= nw) return;
 
   // ---------------- rows ----------------
-  const int nseg = (K + kSegValues - 1) / kSegValues;
+  const uint32_t qx_s = smem_u32(qx), dx_s = smem_u32(dx);
   XSeg xs;
-  if constexpr (kXReg) xs = load_xseg(qx, dx, nb, 0);
-  // row value `v` of CTA row `rr` (held by one lane): written to y, or (cross-GPU sum)
-  // staged on every rank
+  if constexpr (kXReg) xs = load_xseg_s(qx_s, dx_s, nb, 0);
+  // row value `v` of CTA row `rr`: written to y (+ residual), or (cross-GPU sum) staged on
+  // every rank.  A row is emitted by exactly one thread, which reads its residual first
+  // (the residual may alias y).
   auto emit = [&](int rr, float v) {
     if constexpr (kAllreduce) {
       const size_t at = ((size_t)(fz.ar_epoch & 1u) * fz.ar_world + fz.ar_rank) * N + r0 + rr;
       for (int p = 0; p < fz.ar_world; ++p) fz.ar_stage[p][at] = v;
     } else {
-      y[r0 + rr] = v;
+      y[r0 + rr] = fz.residual ? __fadd_rn(fz.residual[r0 + rr], v) : v;
     }
   };
-  for (int t = 0, j = warp; j < nslots; ++t, j += nw) {
-    cp_async_wait(depth - 1);  // this thread's copies of slot t have landed
-    __syncwarp();              // ... and every lane's
-    const uint8_t* sl = ring + (size_t)(t % depth) * geo.slot_bytes;
-    const int row0 = j * rps;
-    const int rows = min(rps, nrows - row0);
-    // residual rows of the slot, read before anything of the slot is written (the
-    // residual may alias y; row i belongs to lane i)
-    float res = 0.0f;
-    if (!kAllreduce && fz.residual && lane < rows) res = fz.residual[r0 + row0 + lane];
-    float mine = 0.0f;
-    for (int i = 0; i < rows; i += 2) {
-      const bool has_b = i + 1 < rows;
-      const uint8_t* wa = sl + (size_t)i * S;
-      const uint8_t* wb = has_b ? wa + S : wa;
-      float ta, tb;
-      if constexpr (kXReg) {
-        seg_terms2(wa, wb, has_b, K, 0, xs, ta, tb);
-      } else {
-        ta = 0.0f;
-        tb = 0.0f;
+
+  // Phase 1, all mode: items of R rows x one 2048-value segment over the 16 warps (R = 4,
+  // 2 or 1, the largest that still gives every warp about one item); each lane sums its
+  // two block terms per row and one transposing reduction gives the R row sums.
+  // Segment sums of longer rows are added in segment order through shared memory.
+  auto all_items = [&](auto rtag) {
+    constexpr int R = decltype(rtag)::value;
+    const int nitems = ((p1_rows + R - 1) / R) * nseg;
+    for (int it = warp; it < nitems; it += kStreamWarps) {
+      const int grp = nseg == 1 ? it : it / nseg;
+      const int sg = it - grp * nseg, rb = grp * R;
+      const int nr = min(R, p1_rows - rb);
+      XSeg xsg;
+      if constexpr (kXReg) xsg = xs;
+      else xsg = load_xseg_s(qx_s, dx_s, nb, sg);
+      uint32_t ra[R];
+#pragma unroll
+      for (int q = 0; q < R; ++q) ra[q] = rowaddr[q < nr ? rb + q : rb];
+      float v[R];
+#pragma unroll
+      for (int q = 0; q < R; ++q) v[q] = q < nr ? seg_terms1_s(ra[q], K, sg, xsg) : 0.0f;
+      const float tot = transpose_reduce<R>(v, lane);
+      const int q = mr_index<R>(lane);
+      if ((lane & (32 / R - 1)) == 0 && q < nr) {  // one lane per row
+        if (nseg == 1) emit(rb + q, tot);
+        else part[sg * p1_rows + rb + q] = tot;
+      }
+    }
+  };
+
+  if (!own) {
+    const int rowsegs = p1_rows * nseg;
+    if (rowsegs > 2 * kStreamWarps) all_items(std::integral_constant<int, 4>{});
+    else if (rowsegs > kStreamWarps) all_items(std::integral_constant<int, 2>{});
+    else all_items(std::integral_constant<int, 1>{});
+    if (nseg > 1) {
+      __syncthreads();  // every segment sum is in shared memory
+      for (int rr = threadIdx.x; rr < p1_rows; rr += kStreamThreads) {
+        float v = part[rr];
+        for (int sg = 1; sg < nseg; ++sg) v = __fadd_rn(v, part[sg * p1_rows + rr]);
+        emit(rr, v);
+      }
+    }
+  } else if (warp < nw) {
+    // Own mode: this warp's slots stream through its private ring and are consumed in
+    // order, each slot refilled with the warp's slot `depth` further on as soon as it is
+    // done (the first `depth` were prefetched before the dependency wait).
+    const uint32_t ring_s = smem_u32(ring);
+    int pos = 0;  // ring position of slot t (t % depth)
+    for (int t = 0, j = warp; j < nslots; ++t, j += nw) {
+      cp_async_wait(depth - 1);  // this thread's copies of slot t have landed
+      __syncwarp();              // ... and every lane's
+      const uint32_t sl = ring_s + (uint32_t)(pos * geo.slot_bytes);
+      pos = pos + 1 == depth ? 0 : pos + 1;
+      const int row0 = j * rps;
+      const int rows = min(rps, nrows - row0);
+      float mine = 0.0f;
+      for (int i = 0; i < rows; i += 2) {
+        const bool has_b = i + 1 < rows;
+        const uint32_t wa = sl + (uint32_t)(i * (int)S);
+        const uint32_t wb = has_b ? wa + (uint32_t)S : wa;
+        float ta = 0.0f, tb = 0.0f;
         for (int sg = 0; sg < nseg; ++sg) {
-          const XSeg xsg = load_xseg(qx, dx, nb, sg);
+          XSeg xsg;
+          if constexpr (kXReg) xsg = xs;
+          else xsg = load_xseg_s(qx_s, dx_s, nb, sg);
           float pa, pb;
-          seg_terms2(wa, wb, has_b, K, sg, xsg, pa, pb);
+          seg_terms2_s(wa, wb, has_b, K, sg, xsg, pa, pb);
           ta = __fadd_rn(ta, pa);
           tb = __fadd_rn(tb, pb);
         }
+        warp_sum2(ta, tb);
+        if (lane == i) mine = ta;
+        if (lane == i + 1) mine = tb;
       }
-      warp_sum2(ta, tb);
-      if (lane == i) mine = ta;
-      if (lane == i + 1) mine = tb;
+      __syncwarp();  // every lane is done with the slot before it is refilled
+      issue(t + depth);
+      if (lane < rows) emit(row0 + lane, mine);
     }
-    __syncwarp();  // every lane is done with the slot before it is refilled
-    issue(t + depth);
-    if (lane < rows) emit(row0 + lane, (!kAllreduce && fz.residual) ? __fadd_rn(res, mine) : mine);
+    cp_async_wait(0);  // no copy of this warp outlives it (the trailing groups are empty)
   }
-  cp_async_wait(0);  // no copy of this warp outlives it (the trailing groups are empty)
   if constexpr (kAllreduce) {
     // ---- cross-GPU sum of this CTA's rows (the same row range on every rank) ----
-    asm volatile("bar.sync 1, %0;" ::"r"(nw * 32) : "memory");  // all rows staged
+    __syncthreads();  // all rows staged
     if (threadIdx.x == 0) {
       int ok = 1;
       __threadfence_system();  // the peer stores of this CTA before its flags
@@ -422,14 +489,14 @@ gemv_q8_0_stream_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, 
       if (!ok) atomicOr(&g_gemv_fault, 2u);
       s_ok = ok;
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(nw * 32) : "memory");
+    __syncthreads();
     if (!s_ok) {  // a peer never arrived: this CTA's rows read as NaN
       const float nan = __int_as_float(0x7fc00000);
-      for (int rr = threadIdx.x; rr < nrows; rr += nw * 32) y[r0 + rr] = nan;
+      for (int rr = threadIdx.x; rr < nrows; rr += kStreamThreads) y[r0 + rr] = nan;
       return;
     }
     const float* stage = fz.ar_stage[fz.ar_rank] + (size_t)(fz.ar_epoch & 1u) * fz.ar_world * N;
-    for (int rr = threadIdx.x; rr < nrows; rr += nw * 32) {
+    for (int rr = threadIdx.x; rr < nrows; rr += kStreamThreads) {
       float v = __ldcv(stage + r0 + rr);  // rank 0's rows, then rank 1's, ... (fixed order)
       for (int p = 1; p < fz.ar_world; ++p) v = __fadd_rn(v, __ldcv(stage + (size_t)p * N + r0 + rr));
       y[r0 + rr] = fz.residual ? __fadd_rn(fz.residual[r0 + rr], v) : v;
@@ -472,7 +539,11 @@ StreamGeo stream_geometry(int64_t k, int64_t S) {
 }
 
 size_t stream_smem_bytes(const StreamGeo& g, int64_t k) {
-  return (size_t)g.nw * g.depth * g.slot_bytes + round16(k) + round16(4 * (k / kQK));
+  const int64_t nseg = (k + kSegValues - 1) / kSegValues;
+  const size_t p1_cap = (size_t)g.nw * g.depth * g.rps;  // prefetched rows at most
+  const size_t part = nseg > 1 ? (size_t)nseg * p1_cap * sizeof(float) : 0;
+  return (size_t)g.nw * g.depth * g.slot_bytes + round16(k) + round16(4 * (k / kQK)) + part +
+         p1_cap * sizeof(uint32_t);
 }
 
 template <bool kAllreduce, bool kXReg>

@@ -47,41 +47,6 @@ struct MrowGeo {
   int rps = 0, nw = 0, slot_bytes = 0;
 };
 
-// Sum over the warp of v[m], m < MR, leaving in every lane the total of row mr_index(lane).
-template <int MR>
-__device__ __forceinline__ float transpose_reduce(float (&v)[MR], int lane) {
-#pragma unroll
-  for (int L = 0; L < 5; ++L) {
-    const int o = 16 >> L;
-    const int c = MR >> L;  // values held before this level
-    if (c > 1) {
-      const bool up = (lane & o) != 0;
-#pragma unroll
-      for (int i = 0; i < MR / 2; ++i) {
-        if (i < c / 2) {
-          const float send = up ? v[i] : v[i + c / 2];
-          const float keep = up ? v[i + c / 2] : v[i];
-          v[i] = keep + __shfl_xor_sync(kFull, send, o);
-        }
-      }
-    } else {
-      v[0] += __shfl_xor_sync(kFull, v[0], o);
-    }
-  }
-  return v[0];
-}
-
-template <int MR>
-__device__ __forceinline__ int mr_index(int lane) {
-  int m = 0;
-#pragma unroll
-  for (int L = 0; L < 5; ++L) {
-    const int c = MR >> L;
-    if (c > 1 && (lane & (16 >> L))) m += c / 2;
-  }
-  return m;
-}
-
 // Block `blk` of a weight row (two 16-byte halves in the lane's half order) and its scale.
 struct WBlock {
   int4 h0, h1;
@@ -120,6 +85,7 @@ gemv_q8_0_mrow_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, in
   uint8_t* ring = smem + (size_t)warp * kMrDepth * geo.slot_bytes;
 
   pdl_launch_dependents();
+  const uint64_t l2pol = l2_evict_first_policy();
   auto issue = [&](int t) {
     const int j = warp + t * nw;
     if (j < nslots) {
@@ -127,7 +93,7 @@ gemv_q8_0_mrow_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, in
       const int units = (min(rps, nrows - row) * (int)S) >> 4;
       const uint8_t* src = W + (size_t)(r0 + row) * S;
       const uint32_t dst = su32(ring + (size_t)(t % kMrDepth) * geo.slot_bytes);
-      for (int u = lane; u < units; u += 32) cp_async16(dst + 16u * u, src + 16 * (size_t)u);
+      for (int u = lane; u < units; u += 32) cp_async16_stream(dst + 16u * u, src + 16 * (size_t)u, l2pol);
     }
     cp_async_commit();
   };
