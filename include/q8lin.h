@@ -108,7 +108,8 @@ enum q8lin_path {
   Q8LIN_PATH_GEMV = 1,        /* M <= 4: register-streaming GEMV */
   Q8LIN_PATH_SMALL_BATCH = 2, /* 2 <= M <= 16 where it wins: dp4a against every row */
   Q8LIN_PATH_INT8_TC = 3,     /* M <= 32: int8 tensor cores, weights on the 128-row side */
-  Q8LIN_PATH_F16_TC = 4       /* M > 32: f16 tensor cores with per-block rescale */
+  Q8LIN_PATH_F16_TC = 4,      /* M > 32: f16 tensor cores with per-block rescale */
+  Q8LIN_PATH_SMALL_BATCH_TC = 5 /* 2 <= M <= 16: mma.sync int8, activations quantized once */
 };
 int q8lin_dispatch_path(int64_t m, int64_t k, int64_t n);
 

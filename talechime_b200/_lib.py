@@ -32,8 +32,9 @@ PATH_GEMV = 1
 PATH_SMALL_BATCH = 2
 PATH_INT8_TC = 3
 PATH_F16_TC = 4
+PATH_SMALL_BATCH_TC = 5
 PATH_NAMES = {PATH_STREAM_GEMV: "stream_gemv", PATH_GEMV: "gemv", PATH_SMALL_BATCH: "small_batch_dp4a",
-              PATH_INT8_TC: "int8_tc", PATH_F16_TC: "f16_tc"}
+              PATH_INT8_TC: "int8_tc", PATH_F16_TC: "f16_tc", PATH_SMALL_BATCH_TC: "small_batch_mma"}
 
 
 class Op(ctypes.Structure):

@@ -95,11 +95,30 @@ bool use_gemv(int64_t m, int64_t k) {
   return m >= 1 && m <= kGemvPathMaxM && gemv_smem_bytes((int)m, k) <= kGemvSmemLimit;
 }
 bool use_skinny(int64_t m) { return m > kGemvPathMaxM && m <= kSkinnyMaxM; }
+// Small batches on mma.sync int8 (gemm_mma.cu), activations quantized once per call: from
+// M = 12 where the activations fit in shared memory beside the rings (K <= 2048 at
+// M = 16).  Measured on B200 in CUDA graphs (us per call, this path vs the dp4a kernel):
+// qkv 2048->6144 M=12 12.3 vs 13.6, M=16 13.4 vs 16.4; o 2048->2048 M=12 7.7 vs 8.6,
+// M=16 8.6 vs 10.4; gate_up 2048->12288 M=16 21.2 vs 23.1 (M=12 20.0 vs 19.1).  Below
+// M = 12 the quantization launch (two dependency releases, ~2.3 us) outweighs it
+// (qkv M=4 9.4 vs 6.8).  Q8LIN_SMALL_MMA=0 turns it off, =1 takes it from M = 2
+// (comparisons).
+constexpr int kMmaMinM = 12;
+bool use_mma(int64_t m, int64_t k) {
+  static const int mode = [] {
+    const char* v = getenv("Q8LIN_SMALL_MMA");
+    return v ? (v[0] == '0' ? 0 : (v[0] == '1' ? 2 : 1)) : 1;
+  }();
+  if (mode == 0) return false;
+  return (mode == 2 || m >= kMmaMinM) && mma_applies(m, k);
+}
 
 // (Where the kernel choice depends on N -- M = 3, 4 at K <= 2048 -- both candidates need
 // no workspace, so the size needs only M and K.)
 size_t workspace_bytes(int64_t m, int64_t k) {
-  if (m <= 0 || use_mrow(m, k, INT64_MAX / k) || use_gemv(m, k)) return 0;
+  if (m <= 0) return 0;
+  if (use_mma(m, k)) return gemm_mma_workspace_bytes(m, k);
+  if (use_mrow(m, k, INT64_MAX / k) || use_gemv(m, k)) return 0;
   if (use_skinny(m)) return gemm_skinny_workspace_bytes(m, k);
   return gemm_tc_workspace_bytes(m, k);
 }
@@ -314,6 +333,17 @@ int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
   if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
+  if (use_mma(m, w->k)) {
+    const size_t need = workspace_bytes(m, w->k);
+    if (!workspace || workspace_bytes_avail < need)
+      return fail(Q8LIN_ERR_WORKSPACE, "workspace of " + std::to_string(workspace_bytes_avail) +
+                                           " bytes is smaller than the " + std::to_string(need) + " bytes needed for M=" +
+                                           std::to_string(m));
+    if (reinterpret_cast<uintptr_t>(workspace) % kAlign) return fail(Q8LIN_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+    e = launch_gemm_mma(*w, x, workspace, y, m, s);
+    if (e != cudaSuccess) return cuda_fail(e, "small-batch tensor-core launch");
+    return Q8LIN_OK;
+  }
   if (use_mrow(m, w->k, w->n)) {
     e = launch_gemv_mrow(*w, x, y, (int)m, s);
     if (e != cudaSuccess) return cuda_fail(e, "small-batch gemv launch");
@@ -421,6 +451,7 @@ uint64_t q8lin_wait_limit_ns(void) { return wait_limit_ns(); }
 int q8lin_dispatch_path(int64_t m, int64_t k, int64_t n) {
   if (m <= 0 || k <= 0 || n <= 0 || k % kQK) return -1;
   // the order of q8lin_forward_ws
+  if (use_mma(m, k)) return Q8LIN_PATH_SMALL_BATCH_TC;
   if (use_mrow(m, k, n)) return Q8LIN_PATH_SMALL_BATCH;
   if (use_gemv(m, k)) return (m == 1 && stream_applies(k)) ? Q8LIN_PATH_STREAM_GEMV : Q8LIN_PATH_GEMV;
   if (use_skinny(m)) return Q8LIN_PATH_INT8_TC;

@@ -44,6 +44,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 __global__ void embed_rows_kernel(const uint8_t* __restrict__ packed, int64_t S, int K, int vocab,
                                   const int* __restrict__ tokens, int n, float* __restrict__ out) {
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   pdl_wait();
   const int r = blockIdx.x;
   if (r < n) {
@@ -54,12 +55,12 @@ __global__ void embed_rows_kernel(const uint8_t* __restrict__ packed, int64_t S,
     for (int i = threadIdx.x; i < K; i += blockDim.x)
       out[(size_t)r * K + i] = __fmul_rn((float)(int8_t)row[i], __half2float(d[i >> 5]));
   }
-  pdl_launch_dependents();
 }
 
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float eps, int n,
                                float* __restrict__ y) {
   __shared__ float red[32];
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   pdl_wait();
   const float* xr = x + (size_t)blockIdx.x * n;
   float s = 0.0f;
@@ -68,7 +69,6 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum2, (float)n), eps));
   for (int i = threadIdx.x; i < n; i += blockDim.x)
     y[(size_t)blockIdx.x * n + i] = __fmul_rn(__fdiv_rn(xr[i], m), w[i]);
-  pdl_launch_dependents();
 }
 
 // qkv[(Hq + 2 Hkv) * D] of the current token; cos/sin [max_t][D/2]; caches [Hkv][max_t][D].
@@ -76,6 +76,7 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, const int* __restr
                                const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                float* __restrict__ kc, float* __restrict__ vc, int Hq, int Hkv, int D, int max_t,
                                float* __restrict__ q_out) {
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   pdl_wait();
   const int pos = *pos_dev;
   const int half = D / 2;
@@ -99,7 +100,6 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, const int* __restr
       vc[((size_t)hv * max_t + pos) * D + i] = qkv[(size_t)head * D + i];
     }
   }
-  pdl_launch_dependents();
 }
 
 // grid (Hq, splits); block kAttnWarps warps.  D = 128: four dims per lane.
@@ -112,6 +112,7 @@ attention_decode_kernel(const float* __restrict__ q, const float* __restrict__ k
   __shared__ float wm[kAttnWarps], wl[kAttnWarps];
   __shared__ float wacc[kAttnWarps][D];
   __shared__ int last;
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   pdl_wait();
   const int h = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
   const int hk = h / (Hq / Hkv);
@@ -185,7 +186,6 @@ attention_decode_kernel(const float* __restrict__ q, const float* __restrict__ k
     }
     if (threadIdx.x == 0) cnt[h] = 0;
   }
-  pdl_launch_dependents();
 }
 
 // ---------------------------------------------------------------------------------
@@ -424,10 +424,10 @@ rope_attention_kernel(const float* __restrict__ qkv, const int* __restrict__ pos
 }
 
 __global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, int64_t n) {
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   pdl_wait();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) x[i] = __fadd_rn(x[i], y[i]);
-  pdl_launch_dependents();
 }
 
 // Greedy argmax: per-CTA (value, index) partials, the last CTA reduces them (lowest
@@ -437,6 +437,7 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n, float* __
   __shared__ float sv[32];
   __shared__ int si[32];
   __shared__ int last;
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   pdl_wait();
   float bv = -INFINITY;
   int bi = n;
@@ -471,7 +472,6 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n, float* __
     if (pos_dev) *pos_dev += 1;
     *cnt = 0;
   }
-  pdl_launch_dependents();
 }
 
 cudaLaunchConfig_t pdl_cfg(dim3 grid, dim3 block, cudaStream_t s, cudaLaunchAttribute* attr) {

@@ -166,6 +166,7 @@ gemm_q8_0_skinny_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_
                         const __grid_constant__ CUtensorMap map_dx, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
   const int n0 = tile * kRows;
@@ -338,6 +339,7 @@ __global__ void quantize_rows_i8t_kernel(const float* __restrict__ x, int M, int
                                          float* __restrict__ dxT) {
   const int nb = K >> 5;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   pdl_wait();
   if (i < (int64_t)Mp * nb) {
     const int b = (int)(i / Mp), m = (int)(i % Mp);
@@ -357,7 +359,6 @@ __global__ void quantize_rows_i8t_kernel(const float* __restrict__ x, int M, int
       dxT[(size_t)b * Mp + m] = 0.0f;
     }
   }
-  pdl_launch_dependents();
 }
 
 // y[m][n] = sum over splits, in split order, of the split-K partials
@@ -366,6 +367,7 @@ __global__ void quantize_rows_i8t_kernel(const float* __restrict__ x, int M, int
 __global__ void skinny_split_reduce_kernel(const float* __restrict__ part, int splits, int Np, int M, int N,
                                            float* __restrict__ y) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   pdl_wait();  // the matmul's partials
   if (i < (int64_t)M * N) {
     const int m = (int)(i / N), n = (int)(i % N);
@@ -374,7 +376,6 @@ __global__ void skinny_split_reduce_kernel(const float* __restrict__ part, int s
     for (int sp = 1; sp < splits; ++sp) sum += src[(size_t)sp * Np * kRows];
     y[i] = sum;
   }
-  pdl_launch_dependents();
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -434,6 +435,20 @@ cudaError_t launch_np(const CUtensorMap& mw, const CUtensorMap& mx, const CUtens
 }
 
 }  // namespace
+
+cudaError_t launch_quantize_rows_i8t(const float* x, int M, int Mp, int K, int8_t* qx, float* dxT, cudaStream_t s) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  const int64_t work = (int64_t)Mp * (K / kQK);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((work + 255) / 256));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, quantize_rows_i8t_kernel, x, M, Mp, K, qx, dxT);
+}
 
 size_t gemm_skinny_workspace_bytes(int64_t m, int64_t k) {
   const int Np = np_of(m);

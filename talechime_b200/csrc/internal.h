@@ -121,6 +121,16 @@ cudaError_t read_tc_fault(unsigned int* flags, bool clear);
 // x to int8 + transposed scales in `workspace`, then the kind::i8 matmul (split-K with
 // partial sums in the workspace).  Fault word bit 2.
 constexpr int kSkinnyMaxM = 32;
+// x [M][K] f32 -> int8 [M][K] and scales dxT[K/32][Mp] (rows M .. Mp - 1 of dxT zero)
+cudaError_t launch_quantize_rows_i8t(const float* x, int M, int Mp, int K, int8_t* qx, float* dxT, cudaStream_t s);
+// small batches on mma.sync int8 tensor cores (gemm_mma.cu): activations quantized once
+// into the workspace, then the weights streamed in 16-row x 256-value units
+constexpr int kMmaMaxM = 16;
+constexpr size_t kMmaMaxSmem = 110 * 1024;
+bool mma_applies(int64_t m, int64_t k);
+size_t gemm_mma_workspace_bytes(int64_t m, int64_t k);
+cudaError_t launch_gemm_mma(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
+                            cudaStream_t s);
 size_t gemm_skinny_workspace_bytes(int64_t m, int64_t k);
 cudaError_t launch_gemm_skinny(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
                                cudaStream_t s);

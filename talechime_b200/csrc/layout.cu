@@ -83,6 +83,7 @@ __global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t m, int
                                      float* __restrict__ d_f32) {
   const int64_t nb = k / kQK;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   pdl_wait();
   if (i < m * nb) {
     const float4* src = reinterpret_cast<const float4*>(x + i * kQK);
@@ -98,7 +99,6 @@ __global__ void quantize_rows_kernel(const float* __restrict__ x, int64_t m, int
     if (d_f16) d_f16[i] = __half_as_ushort(dh);
     if (d_f32) d_f32[i] = __half2float(dh);
   }
-  pdl_launch_dependents();
 }
 
 inline unsigned blocks_for(int64_t work, int threads) {

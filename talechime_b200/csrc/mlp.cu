@@ -18,6 +18,7 @@ namespace {
 __global__ void swiglu4_kernel(const float* __restrict__ gu, int64_t m, int64_t inter, float* __restrict__ h) {
   const int64_t q = inter / 4;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   pdl_wait();
   if (i < m * q) {
     const int64_t r = i / q, c = i - r * q;
@@ -26,17 +27,16 @@ __global__ void swiglu4_kernel(const float* __restrict__ gu, int64_t m, int64_t 
     reinterpret_cast<float4*>(h + r * inter)[c] =
         make_float4(silu_mul(g.x, u.x), silu_mul(g.y, u.y), silu_mul(g.z, u.z), silu_mul(g.w, u.w));
   }
-  pdl_launch_dependents();
 }
 
 __global__ void swiglu1_kernel(const float* __restrict__ gu, int64_t m, int64_t inter, float* __restrict__ h) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   pdl_wait();
   if (i < m * inter) {
     const int64_t r = i / inter, c = i - r * inter;
     h[i] = silu_mul(gu[r * 2 * inter + c], gu[r * 2 * inter + inter + c]);
   }
-  pdl_launch_dependents();
 }
 
 }  // namespace

@@ -93,8 +93,12 @@ def test_python_surface_rejects_cpu_device():
     (7, 6144, 2048, "int8_tc"),          # ... from M = 7 the int8 tensor cores
     (3, 2048, 4096, "small_batch_dp4a"), # M = 3, 4 with N*K >= 8M weights
     (4, 2048, 2048, "gemv"),             # ... but not below
-    (5, 2048, 2048, "small_batch_dp4a"), # K <= 2048, 5 <= M <= 16
-    (16, 2048, 12288, "small_batch_dp4a"),
+    (5, 2048, 2048, "small_batch_dp4a"), # K <= 2048, 5 <= M <= 11
+    (11, 2048, 12288, "small_batch_dp4a"),
+    (12, 2048, 2048, "small_batch_mma"),  # 12 <= M <= 16 where x fits in shared memory
+    (16, 2048, 12288, "small_batch_mma"),
+    (16, 4096, 2048, "int8_tc"),          # ... not at K = 4096 (x does not fit)
+    (12, 6144, 2048, "int8_tc"),
     (17, 2048, 2048, "int8_tc"),
     (32, 6144, 2048, "int8_tc"),
     (33, 2048, 2048, "f16_tc"),
