@@ -162,14 +162,18 @@ namespace {
 std::mutex g_attr_mu;
 }  // namespace
 
+// configured[dev]: the largest dynamic shared memory already set for fn on that device.
+// Read with an acquire load on every launch (no lock once configured); the first call per
+// device and size sets the attribute under a lock and publishes it with a release store.
 cudaError_t ensure_smem(const void* fn, int* configured, int device, size_t smem, bool max_carveout) {
   const int dev = (device >= 0 && device < 128) ? device : 0;
+  if ((int)smem <= __atomic_load_n(&configured[dev], __ATOMIC_ACQUIRE)) return cudaSuccess;
   std::lock_guard<std::mutex> lock(g_attr_mu);
-  if ((int)smem <= configured[dev]) return cudaSuccess;
+  if ((int)smem <= __atomic_load_n(&configured[dev], __ATOMIC_RELAXED)) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess && max_carveout)
     e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-  if (e == cudaSuccess) configured[dev] = (int)smem;
+  if (e == cudaSuccess) __atomic_store_n(&configured[dev], (int)smem, __ATOMIC_RELEASE);
   return e;
 }
 

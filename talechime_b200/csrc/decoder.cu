@@ -531,13 +531,8 @@ cudaError_t launch_rope_attention(const float* qkv, const int* pos, const float*
                                   float* vc, int hq, int hkv, int max_t, float* out, int device, cudaStream_t s,
                                   bool pos_ready) {
   static int configured[128] = {0};
-  const int dev = (device >= 0 && device < 128) ? device : 0;
-  if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(rope_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)sizeof(RaSmem));
-    if (e != cudaSuccess) return e;
-    configured[dev] = 1;
-  }
+  cudaError_t e0 = ensure_smem((const void*)rope_attention_kernel, configured, device, sizeof(RaSmem), false);
+  if (e0 != cudaSuccess) return e0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kRaCluster, (unsigned)hq);
   cfg.blockDim = dim3(kRaThreads);

@@ -415,12 +415,8 @@ cudaError_t launch_np(const CUtensorMap& mw, const CUtensorMap& mx, const CUtens
                       int tiles, int dev, cudaStream_t s) {
   const size_t smem = sizeof(Smem) + 1024;
   static int configured[128] = {0};
-  if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_q8_0_skinny_kernel<NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    configured[dev] = 1;
-  }
+  cudaError_t e0 = ensure_smem((const void*)gemm_q8_0_skinny_kernel<NP>, configured, dev, smem, false);
+  if (e0 != cudaSuccess) return e0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)tiles, (unsigned)p.splits);
   cfg.blockDim = dim3(kThreads);

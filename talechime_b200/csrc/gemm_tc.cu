@@ -649,11 +649,9 @@ cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspac
   // 2. tensor-core matmul
   const size_t smem = gemm_tc_smem_bytes();
   static int configured[128] = {0};
-  const int dev = (w.device >= 0 && w.device < 128) ? w.device : 0;
-  if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_q8_0_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    cudaError_t e = ensure_smem((const void*)gemm_q8_0_tc_kernel, configured, w.device, smem, false);
     if (e != cudaSuccess) return e;
-    configured[dev] = 1;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM), (unsigned)splits);

@@ -29,6 +29,8 @@
 #include <mutex>
 #include <string>
 
+#include <cuda.h>
+
 #include "common.cuh"
 #include "internal.h"
 #include "q8lin.h"
@@ -46,17 +48,39 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 constexpr int kMaxDevices = 128;
 std::mutex g_addr_mu;
 void* g_addr[kMaxDevices] = {};
+CUcontext g_ctx[kMaxDevices] = {};  // the context g_addr belongs to
 
-// Device address of g_noalloc_scratch on `device` (which must be current).
+// The calling thread's current CUDA context (the driver entry point is resolved once).
+CUcontext current_context() {
+  using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+  static const CtxGetCurrentFn fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (CtxGetCurrentFn) nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(ptr);
+  }();
+  CUcontext c = nullptr;
+  if (fn && fn(&c) != CUDA_SUCCESS) c = nullptr;
+  return c;
+}
+
+// Device address of g_noalloc_scratch on `device` (which must be current).  Cached per
+// device together with the context it was looked up in: after a device reset (a new
+// primary context, the module loaded again at possibly another address) it is looked up
+// again.
 int scratch_address(int device, void** out) {
   if (device < 0 || device >= kMaxDevices)
     return fail(Q8LIN_ERR_DEVICE, "device ordinal " + std::to_string(device) + " beyond the supported range");
   std::lock_guard<std::mutex> lock(g_addr_mu);
-  if (!g_addr[device]) {
+  const CUcontext ctx = current_context();
+  if (!g_addr[device] || !ctx || g_ctx[device] != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-allocation scratch)");
     g_addr[device] = p;
+    g_ctx[device] = current_context();  // the lookup may have created the context
   }
   *out = g_addr[device];
   return Q8LIN_OK;
