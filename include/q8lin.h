@@ -90,8 +90,9 @@ int q8lin_weight_dequantize(const q8lin_weight* w, float* out, q8lin_stream_t st
 int q8lin_weight_export_gguf(const q8lin_weight* w, void* out_blocks, q8lin_stream_t stream);
 
 /* Workspace bytes q8lin_forward_ws needs for M rows: 0 where a GEMV kernel serves M
- * (M <= 4, and the small-batch kernel's range, see q8lin_dispatch_path); on the int8
- * tensor-core path (M <= 32) the int8 activations [M][K], transposed f32 scales and
+ * (M <= 4, and the dp4a small-batch kernel's range, see q8lin_dispatch_path); on the
+ * mma.sync small-batch path (12 <= M <= 16 where it applies) the int8 activations
+ * [M][K] and transposed f32 scales; on the int8 tensor-core path (M <= 32) the same plus
  * the split-K partial sums; for larger M the activations as f16 integers [M][K],
  * transposed f32 scales and one wave of split-K partial tiles.  Regions are 256-byte
  * aligned. */
