@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define Q8LIN_VERSION 2
+#define Q8LIN_VERSION 3
 #define Q8LIN_QK 32          /* values per Q8_0 block */
 #define Q8LIN_BLOCK_BYTES 34 /* GGUF block: f16 d + int8 qs[32] */
 
@@ -268,14 +268,17 @@ int q8lin_argmax(const float* logits, int64_t n, void* workspace, size_t workspa
  * order (deterministic; bit-identical to a two-rank NCCL sum).  Replaces the partial
  * down projection + all-reduce of the tensor-parallel MLP (crates/voxcpm/src/transformer.rs
  * :147-150 split over GPUs).  Buffers: one staging buffer of
- * q8lin_allreduce_stage_bytes(N, world) and one flag buffer of
- * q8lin_allreduce_flag_bytes(world) per rank, allocated with q8lin_peer_alloc (zeroed; its
- * IPC handle, Q8LIN_IPC_HANDLE_BYTES bytes, is exchanged out of band and opened on the other
- * ranks with q8lin_peer_open).  stage_n: the N the staging buffers were sized for (a weight
- * with more rows is rejected).  stage_ptrs / flag_ptrs: DEVICE arrays of `world` pointers,
- * entry r = rank r's buffer as mapped on this GPU.  epoch: the call count, 1, 2, ... (every
- * rank passes the same value; all ranks must make every call).  A rank that never arrives
- * makes the others time out (fault word bit 1) instead of hanging.
+ * q8lin_allreduce_stage_bytes(N, world) per rank, allocated with q8lin_peer_alloc (zeroed;
+ * its IPC handle, Q8LIN_IPC_HANDLE_BYTES bytes, is exchanged out of band and opened on the
+ * other ranks with q8lin_peer_open).  Every staged value travels with the call's epoch in
+ * one 64-bit word, so a rank knows a peer's row has arrived when it reads that epoch: no
+ * fence and no flag.  stage_n: the N the staging buffers were sized for (a weight with
+ * more rows is rejected).  stage_ptrs: DEVICE array of `world` pointers, entry r = rank
+ * r's buffer as mapped on this GPU.  flag_ptrs: not read since version 3 (may be NULL;
+ * q8lin_allreduce_flag_bytes is kept for callers of version 2).  epoch: the call count,
+ * 1, 2, ... (every rank passes the same value; all ranks must make every call).  A rank
+ * that never arrives makes the others time out (fault word bit 1, NaN rows) instead of
+ * hanging.
  */
 #define Q8LIN_IPC_HANDLE_BYTES 64
 int q8lin_peer_alloc(int device, size_t bytes, void** ptr, void* ipc_handle);

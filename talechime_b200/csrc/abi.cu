@@ -580,7 +580,8 @@ int q8lin_peer_free(int device, void* ptr) {
 }
 
 size_t q8lin_allreduce_stage_bytes(int64_t n, int32_t world) {
-  return (n > 0 && world > 0) ? (size_t)2 * (size_t)world * (size_t)n * sizeof(float) : 0;
+  // [2 halves][world][n] tagged words: the epoch of the call next to the f32 value
+  return (n > 0 && world > 0) ? (size_t)2 * (size_t)world * (size_t)n * sizeof(unsigned long long) : 0;
 }
 
 size_t q8lin_allreduce_flag_bytes(int32_t world) {
@@ -599,7 +600,7 @@ int q8lin_forward_allreduce(const q8lin_weight* w, const float* x, float* y, int
   if (w->k > kFusedMaxK) return fail(Q8LIN_ERR_SHAPE, "the fused all-reduce needs K <= 8192");
   if (world < 1 || rank < 0 || rank >= world) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "rank must lie in [0, world)");
   if (epoch == 0) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "epoch counts calls from 1");
-  if (!x || !y || (world > 1 && (!stage_ptrs || !flag_ptrs)))
+  if (!x || !y || (world > 1 && !stage_ptrs))
     return fail(Q8LIN_ERR_INVALID_ARGUMENT, "x, y and (world > 1) the peer pointer arrays must be non-null");
   if (!aligned16(x) || !aligned16(y)) return fail(Q8LIN_ERR_ALIGNMENT, "x and y must be 16-byte aligned");
   if (residual && (reinterpret_cast<uintptr_t>(residual) & 3u))
@@ -609,7 +610,7 @@ int q8lin_forward_allreduce(const q8lin_weight* w, const float* x, float* y, int
   if (!guard.ok()) return fail(Q8LIN_ERR_CUDA, "cudaSetDevice failed");
   GemvFusion f;
   f.residual = residual;
-  f.ar_stage = reinterpret_cast<float* const*>(stage_ptrs);
+  f.ar_stage = reinterpret_cast<unsigned long long* const*>(stage_ptrs);
   f.ar_flags = reinterpret_cast<unsigned* const*>(flag_ptrs);
   f.ar_rank = rank;
   f.ar_world = world;

@@ -73,16 +73,16 @@ struct GemvFusion {
   float eps = 0.0f;
   const float* residual = nullptr;
   // Sum of the output over `ar_world` GPUs (tensor-parallel down projection), fused into
-  // the GEMV: every CTA stores its rows into each rank's staging buffer (peer stores over
-  // NVLink), raises its flag on each rank, waits for the same CTA index of every rank, and
-  // adds the staged rows in rank order.  ar_stage / ar_flags: device arrays of `ar_world`
-  // pointers (this rank's own buffers at index ar_rank); stage[r] holds [2][ar_world][N] f32
-  // (calls alternate halves by epoch parity), flags[r] holds [grid][ar_world] u32.
-  // ar_epoch is a per-call counter starting at 1 and a flag counts once it reaches the
-  // call's epoch, so flags never need resetting; a rank can be at most one call ahead of
-  // a peer's reads (its next reduction waits for that peer's next flag), which the two
-  // staging halves cover.
-  float* const* ar_stage = nullptr;
+  // the GEMV: every CTA stores each of its rows into every rank's staging buffer as one
+  // 64-bit word (epoch << 32 | f32 bits, peer stores over NVLink), then each thread waits
+  // for its rows' words of every rank to carry this call's epoch and adds them in rank
+  // order.  ar_stage: device array of `ar_world` pointers (this rank's own buffer at index
+  // ar_rank); stage[r] holds [2][ar_world][N] u64 (calls alternate halves by epoch
+  // parity).  ar_epoch is a per-call counter starting at 1, so the buffers never need
+  // resetting; a rank can be at most one call ahead of a peer's reads (its next sum waits
+  // for that peer's next words), which the two halves cover.  ar_flags: not read (kept
+  // for the C ABI).
+  unsigned long long* const* ar_stage = nullptr;
   unsigned* const* ar_flags = nullptr;
   int ar_rank = 0;
   int ar_world = 1;

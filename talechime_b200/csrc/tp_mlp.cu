@@ -310,7 +310,7 @@ int q8lin_mlp_tp_forward(q8lin_mlp_tp* t, const float* x, float* y, int64_t m, q
     f.prologue = kPrologueSwiGLU;
     if (t->fused) {
       const uint32_t epoch = t->epoch + 1;
-      f.ar_stage = reinterpret_cast<float* const*>(t->peer_ptrs);
+      f.ar_stage = reinterpret_cast<unsigned long long* const*>(t->peer_ptrs);
       f.ar_flags = reinterpret_cast<unsigned* const*>(t->peer_ptrs + t->world);
       f.ar_rank = t->rank;
       f.ar_world = t->world;

@@ -38,7 +38,7 @@ def test_library_exports_every_header_symbol(lib):
 
 
 def test_version(lib):
-    assert lib.q8lin_version() == 2
+    assert lib.q8lin_version() == 3
 
 
 def test_status_strings(lib):

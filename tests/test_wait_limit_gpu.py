@@ -56,8 +56,11 @@ def test_peer_wait_runs_out_and_reports(oracle_lib, cuda_device):
     assert f & 2, f"fault word {f:#x} lacks the streaming GEMV's bit"
     assert _fault(cuda_device) == 0  # read-and-clear
     assert torch.isnan(y).all()
-    # rank 0's rows were staged and its flag raised on both "ranks" before the wait
-    assert int(flags[0][0].item()) == 1 and int(flags[1][0].item()) == 1
+    # rank 0's rows were staged on both "ranks" as tagged words (epoch 1, half 1) before the
+    # wait for rank 1's words ran out
+    for r in range(world):
+        words = stage[r].view(torch.int64)
+        assert int(words[(1 * world + 0) * n].item()) >> 32 == 1
     # the context is still usable: an ordinary call is exact again
     y2 = q.forward(xd)
     torch.cuda.synchronize()
