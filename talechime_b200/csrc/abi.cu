@@ -339,11 +339,14 @@ int q8lin_forward_ws(const q8lin_weight* w, const float* x, float* y, int64_t m,
   cudaError_t e;
   if (use_mma(m, w->k)) {
     const size_t need = workspace_bytes(m, w->k);
-    if (!workspace || workspace_bytes_avail < need)
-      return fail(Q8LIN_ERR_WORKSPACE, "workspace of " + std::to_string(workspace_bytes_avail) +
-                                           " bytes is smaller than the " + std::to_string(need) + " bytes needed for M=" +
-                                           std::to_string(m));
-    if (reinterpret_cast<uintptr_t>(workspace) % kAlign) return fail(Q8LIN_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+    if (need > 0) {
+      if (!workspace || workspace_bytes_avail < need)
+        return fail(Q8LIN_ERR_WORKSPACE, "workspace of " + std::to_string(workspace_bytes_avail) +
+                                             " bytes is smaller than the " + std::to_string(need) +
+                                             " bytes needed for M=" + std::to_string(m));
+      if (reinterpret_cast<uintptr_t>(workspace) % kAlign)
+        return fail(Q8LIN_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+    }
     e = launch_gemm_mma(*w, x, workspace, y, m, s);
     if (e != cudaSuccess) return cuda_fail(e, "small-batch tensor-core launch");
     return Q8LIN_OK;

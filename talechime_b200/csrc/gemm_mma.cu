@@ -27,6 +27,7 @@
 //     free by then).  Sums are deterministic; their association differs from candle's
 //     sequential loop only in where the chunks meet (f32 summation tolerance).
 #include <cstdint>
+#include <cstdlib>
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -68,8 +69,9 @@ struct MmaArgs {
   const uint8_t* W;  // packed rows, stride S
   int64_t S;
   int N, K, M, Mp;
-  const int8_t* qx;  // [M][K] int8 activations
+  const int8_t* qx;  // [M][K] int8 activations (null: the kernel quantizes x itself)
   const float* dxT;  // [K/32][Mp] their scales
+  const float* x;    // [M][K] f32 activations (when qx is null)
   float* y;          // [M][N]
 };
 
@@ -211,7 +213,7 @@ __global__ void __launch_bounds__(kMmThreads, 2) gemm_q8_0_mma_kernel(const MmaA
   const uint32_t xstride = (uint32_t)a.K + 16u;
   const uint32_t xs = su32(smem) + (uint32_t)kMmRingBytes;
   const uint32_t dxs = xs + (uint32_t)round_up16((int64_t)a.M * xstride);
-  {
+  if (a.qx) {  // quantized once per call by the quantization launch
     const int per_row = a.K >> 4;
     for (int i = threadIdx.x; i < a.M * per_row; i += kMmThreads) {
       const int m = i / per_row, c = i - m * per_row;
@@ -221,6 +223,25 @@ __global__ void __launch_bounds__(kMmThreads, 2) gemm_q8_0_mma_kernel(const MmaA
     for (int i = threadIdx.x; i < dpieces; i += kMmThreads) cp_async16(dxs + 16u * i, a.dxT + 4 * i);
     cp_async_commit();
     cp_async_wait(0);  // (the ring's first units too: they were issued long before)
+    __syncthreads();
+  } else {  // small M*K: every CTA quantizes x itself, one 32-value block per thread
+    for (int i = threadIdx.x; i < a.M * nb; i += kMmThreads) {
+      const int m = i / nb, b = i - m * nb;
+      const float4* src = reinterpret_cast<const float4*>(a.x + (size_t)m * a.K + (size_t)b * 32);
+      float4 v[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[t] = __ldg(src + t);
+      int q[8];
+      __half dh;
+      quantize_block_regs(v, q, dh);
+      const uint32_t d = xs + (uint32_t)m * xstride + 32u * (uint32_t)b;
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(d), "r"(q[0]), "r"(q[1]), "r"(q[2]), "r"(q[3])
+                   : "memory");
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(d + 16u), "r"(q[4]), "r"(q[5]), "r"(q[6]),
+                   "r"(q[7]) : "memory");
+      asm volatile("st.shared.f32 [%0], %1;" ::"r"(dxs + 4u * (uint32_t)(b * a.Mp + m)), "f"(__half2float(dh))
+                   : "memory");
+    }
     __syncthreads();
   }
 
@@ -355,7 +376,24 @@ bool mma_applies(int64_t m, int64_t k) {
   return m >= 2 && m <= kMmaMaxM && k <= (1 << 20) && mma_smem_bytes(m, k) <= kMmaMaxSmem;
 }
 
-// int8 activations [M][K], then their scales [K/32][Mp] (Mp = M rounded up to 16)
+// Whether every CTA quantizes the activations itself instead of a quantization launch
+// before the kernel: where M*K is small (a few blocks per thread) and the CTAs hold
+// several 16-row tiles each, so the quantization overlaps the weight stream.  Measured
+// on B200 (graph-timed, us per call, in-kernel vs launch): gate_up 2048->12288 M=12
+// 17.1 vs 20.1, M=16 18.6 vs 21.3; qkv 2048->6144 M=16 13.4 vs 13.6; but o 2048->2048
+// (one tile per CTA) M=16 14.6 vs 8.7.  Q8LIN_MMA_QUANT=launch / =kernel force one way
+// (comparisons).
+bool mma_quant_in_kernel(int64_t m, int64_t k, int64_t n) {
+  static const int mode = [] {
+    const char* v = getenv("Q8LIN_MMA_QUANT");
+    return v ? (v[0] == 'l' ? 0 : (v[0] == 'k' ? 2 : 1)) : 1;
+  }();
+  if (mode != 1) return mode == 2;
+  return m * k <= kMmaInKernelMaxValues && n >= kMmaInKernelMinN;
+}
+
+// int8 activations [M][K], then their scales [K/32][Mp] (Mp = M rounded up to 16): what
+// the quantization launch writes (the kernel that quantizes x itself leaves it unused)
 size_t gemm_mma_workspace_bytes(int64_t m, int64_t k) {
   return up256_mm((size_t)(m * k)) + up256_mm((size_t)mp_of(m) * (k / kQK) * sizeof(float));
 }
@@ -371,12 +409,18 @@ cudaError_t launch_gemm_mma(const q8lin_weight& w, const float* x, void* workspa
   a.K = (int)w.k;
   a.M = (int)m;
   a.Mp = mp_of(m);
-  a.qx = reinterpret_cast<const int8_t*>(ws);
-  a.dxT = reinterpret_cast<const float*>(ws + up256_mm((size_t)(m * w.k)));
   a.y = y;
-  cudaError_t e = launch_quantize_rows_i8t(x, a.M, a.Mp, a.K, reinterpret_cast<int8_t*>(ws),
-                                           const_cast<float*>(a.dxT), s);
-  if (e != cudaSuccess) return e;
+  a.x = x;
+  if (mma_quant_in_kernel(m, w.k, w.n)) {
+    a.qx = nullptr;
+    a.dxT = nullptr;
+  } else {
+    a.qx = reinterpret_cast<const int8_t*>(ws);
+    a.dxT = reinterpret_cast<const float*>(ws + up256_mm((size_t)(m * w.k)));
+    cudaError_t e = launch_quantize_rows_i8t(x, a.M, a.Mp, a.K, reinterpret_cast<int8_t*>(ws),
+                                             const_cast<float*>(a.dxT), s);
+    if (e != cudaSuccess) return e;
+  }
   return m <= 8 ? launch_mma_t<1>(a, w.device, s) : launch_mma_t<2>(a, w.device, s);
 }
 

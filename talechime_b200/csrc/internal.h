@@ -127,6 +127,8 @@ cudaError_t launch_quantize_rows_i8t(const float* x, int M, int Mp, int K, int8_
 // into the workspace, then the weights streamed in 16-row x 256-value units
 constexpr int kMmaMaxM = 16;
 constexpr size_t kMmaMaxSmem = 110 * 1024;
+constexpr int64_t kMmaInKernelMaxValues = 32768;  // M*K the kernel quantizes itself ...
+constexpr int64_t kMmaInKernelMinN = 8192;        // ... for weights of at least this many rows
 bool mma_applies(int64_t m, int64_t k);
 size_t gemm_mma_workspace_bytes(int64_t m, int64_t k);
 cudaError_t launch_gemm_mma(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,

@@ -1,13 +1,15 @@
 """Small batches on mma.sync int8 (gemm_mma.cu): parity with the candle-CPU oracle.
 
 The path serves 12 <= M <= 16 where the activations fit in shared memory beside the
-weight rings (q8lin_dispatch_path == small_batch_mma); the activations are quantized once
-per call into the workspace (candle's Q8_0 rules) and every output is the sum over
-blocks of ((f32(I) * dw) * dx) (candle-core 0.11.0 QMatMul::forward, called from
+weight rings (q8lin_dispatch_path == small_batch_mma); the activations are quantized with
+candle's Q8_0 rules, once per call into the workspace or -- for small M*K and weights of
+8192 rows or more -- by every CTA into its own shared memory, and every output is the sum
+over blocks of ((f32(I) * dw) * dx) (candle-core 0.11.0 QMatMul::forward, called from
 Linear::forward, crates/voxcpm/src/weights.rs:209-229).  Cases cover partial 16-row
 tiles, a partial last 8-block unit, the regime where a CTA holds more tiles than warps
 (each warp whole tiles) and the one where warps split a tile's units (partials added in
-unit order), determinism, and -- in a child process with Q8LIN_SMALL_MMA=1 -- M = 2..11.
+unit order), determinism, and -- in child processes -- M = 2..11 (Q8LIN_SMALL_MMA=1) and
+each quantization variant forced where the default picks the other (Q8LIN_MMA_QUANT).
 """
 import ctypes
 import os
@@ -27,9 +29,9 @@ pytestmark = pytest.mark.gpu
 CASES = [
     (12, 2048, 2048),    # o, M = 12
     (16, 2048, 6144),    # qkv, M = 16
-    (16, 2048, 12288),   # gate_up, M = 16
+    (16, 2048, 12288),   # gate_up, M = 16 (x quantized in the kernel)
     (13, 2080, 100),     # partial tile (100 rows) and a partial last unit (65 blocks)
-    (14, 2048, 28672),   # 1792 tiles: a CTA holds more tiles than warps
+    (14, 2048, 28672),   # 1792 tiles: a CTA holds more tiles than warps (x in the kernel)
     (15, 512, 48),       # 3 tiles, 2 units each
     (12, 96, 17),        # one 3-block unit, one partial tile
 ]
@@ -66,16 +68,16 @@ def test_mma_path_needs_the_workspace(cuda_device):
         L.q8lin_weight_destroy(h)
 
 
-def test_mma_kernel_below_its_range(cuda_device):
-    """M = 2..11 through the same kernel (forced with Q8LIN_SMALL_MMA=1 in a child
-    process: the switch is read once per process)."""
-    code = textwrap.dedent("""
+def _child_parity(cases, **env_vars):
+    """Run the mma path on `cases` in a child process with the given switches (each is
+    read once per process) and check every case against the oracle."""
+    code = textwrap.dedent(f"""
         import numpy as np, torch
         from talechime_b200 import QMatMul, _lib, synth
         import oracle
         from tests.conftest import assert_close_to_oracle
         dev = torch.device("cuda", 0)
-        for m, k, n in ((2, 2048, 256), (3, 2080, 100), (5, 1024, 333), (8, 2048, 2048), (11, 256, 4100)):
+        for m, k, n in {cases!r}:
             assert _lib.PATH_NAMES[_lib.lib().q8lin_dispatch_path(m, k, n)] == "small_batch_mma"
             w = synth.q8_0_blocks(np.random.default_rng(m + n), n, k)
             q = QMatMul.from_gguf_blocks(w, n, k, device=dev)
@@ -85,6 +87,21 @@ def test_mma_kernel_below_its_range(cuda_device):
         print("ok")
     """)
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, Q8LIN_SMALL_MMA="1", PYTHONPATH=root)
+    env = dict(os.environ, PYTHONPATH=root, **env_vars)
     r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def test_mma_kernel_below_its_range(cuda_device):
+    """M = 2..11 through the same kernel (Q8LIN_SMALL_MMA=1), both quantization variants
+    reached by the default choice ((2, 2048, 8192) quantizes x in the kernel)."""
+    _child_parity(((2, 2048, 256), (3, 2080, 100), (5, 1024, 333), (8, 2048, 2048), (11, 256, 4100),
+                   (2, 2048, 8192)), Q8LIN_SMALL_MMA="1")
+
+
+def test_mma_quantization_variants_forced(cuda_device):
+    """Each quantization variant where the default takes the other: x quantized in every
+    CTA for short weights and partial tiles, and by a separate launch for gate_up."""
+    _child_parity(((12, 2048, 2048), (13, 2080, 100), (15, 512, 48), (12, 96, 17), (16, 1024, 300)),
+                  Q8LIN_MMA_QUANT="kernel")
+    _child_parity(((16, 2048, 12288), (14, 2048, 28672)), Q8LIN_MMA_QUANT="launch")
