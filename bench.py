@@ -441,11 +441,11 @@ def run_tp_mlp(torch, dist, dev, rank: int, world: int, reps: int = 20) -> dict:
 def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, steps: int = 512) -> dict:
     """Config 2: the ~2B Q8_0 decoder (hidden 2048, 28 layers, 16 x 128 heads, SwiGLU 6144,
     RMSNorm, RoPE, f32 KV cache, vocab 73448; talechime_b200/decoder.py), batch 1: a
-    128-token random-id prefix, then `steps` greedy decode steps replayed from one CUDA
-    graph of a step; device time of the decode steps (CUDA events), max over ranks (one
-    independent replica per GPU).  Both step implementations are timed: "fused" (one
-    launch per operation, the default) and "persistent" (one cooperative launch per
-    step)."""
+    128-token random-id prefix run as one batched forward (Q8Decoder.prefill, timed on its
+    own), then `steps` greedy decode steps replayed from one CUDA graph of a step; device
+    time of the decode steps (CUDA events), max over ranks (one independent replica per
+    GPU).  Both step implementations are timed: "fused" (one launch per operation, the
+    default) and "persistent" (one cooperative launch per step)."""
     from talechime_b200.decoder import DecoderConfig, Q8Decoder, synthetic_weights
 
     cfg = DecoderConfig(max_t=prefix + steps)
@@ -461,6 +461,17 @@ def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, step
     # KV cache read per step at position p: layers * 2 * kv_heads * (p + 1) * head_dim * 4
     kv_bytes = sum(cfg.layers * 2 * cfg.kv_heads * (p + 1) * cfg.head_dim * 4 for p in range(prefix, prefix + steps))
     results = {}
+    with torch.cuda.stream(stream):
+        dec.reset(ids[0])
+        dec.prefill(ids)  # warm-up: workspace growth and kernel attributes
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dec.reset(ids[0])
+        e0.record(stream)
+        dec.prefill(ids)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    prefill_ms = e0.elapsed_time(e1)
     for mode in ("fused", "persistent"):
         with torch.cuda.stream(stream):
             dec.reset(ids[0])
@@ -471,9 +482,7 @@ def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, step
             with torch.cuda.graph(graph, stream=stream):
                 dec.step(mode)
             dec.reset(ids[0])
-            for t in ids:  # prefix, one position per replay (the argmax output is overwritten)
-                dec.token.fill_(t)
-                graph.replay()
+            dec.prefill(ids)  # the prefix as one forward; the decode steps continue from it
             torch.cuda.synchronize(dev)
             if world > 1:
                 dist.barrier()
@@ -493,7 +502,9 @@ def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, step
     ms, final_pos = results["fused"]
     msp, _ = results["persistent"]
     out = {"config": "Q8_0 decoder, hidden 2048, 28 layers, 16 x 128 heads (MHA), SwiGLU 6144, RMSNorm, RoPE, "
-                     f"f32 KV cache, vocab 73448; batch 1, {prefix}-token random-id prefix, {steps} greedy steps",
+                     f"f32 KV cache, vocab 73448; batch 1, {prefix}-token random-id prefix (one batched forward), "
+                     f"{steps} greedy steps",
+           "prefix_prefill_ms": prefill_ms, "prefix_prefill_tokens_per_s": prefix / (prefill_ms * 1e-3),
            "tokens_per_s": world * steps / (ms * 1e-3), "ms_per_token": ms / steps,
            "tokens_per_s_persistent": world * steps / (msp * 1e-3), "ms_per_token_persistent": msp / steps,
            "weight_bytes_per_token": wbytes, "kv_bytes_per_token_avg": kv_bytes / steps,
@@ -504,6 +515,61 @@ def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, step
     del dec
     torch.cuda.synchronize(dev)
     return out
+
+
+def run_decoder_prefill(torch, dist, dev, rank: int, world: int, batch: int = 4, tokens: int = 1024,
+                        reps: int = 3) -> dict:
+    """BASELINE configs[3] as a decoder pass: the same ~2B Q8_0 decoder prefills `batch`
+    sequences of `tokens` random ids (M = batch * tokens = 4096 rows through every
+    linear) with everything of the prompt pass -- embedding, RMSNorms, RoPE + KV append,
+    causal attention, residual adds, SwiGLU, final norm, LM head and greedy pick of each
+    sequence's last row (Q8Decoder.prefill).  Device time per pass (CUDA events around the
+    call, which starts by reading the position back), max over ranks (one independent
+    replica per GPU)."""
+    from talechime_b200.decoder import DecoderConfig, Q8Decoder, synthetic_weights
+
+    cfg = DecoderConfig(max_t=tokens)
+    weights = synthetic_weights(cfg, seed=4242 + rank, device=dev)
+    dec = Q8Decoder(cfg, weights, device=dev, batch=batch)
+    del weights
+    gen = torch.Generator()
+    gen.manual_seed(4243)
+    ids = torch.randint(0, cfg.vocab, (batch, tokens), generator=gen)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        dec.reset()
+        dec.prefill(ids)  # warm-up
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        times = []
+        for _ in range(reps):
+            dec.reset()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            dec.prefill(ids)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            times.append(e0.elapsed_time(e1))
+    ms = statistics.median(times)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    m = batch * tokens
+    H = cfg.hidden
+    per_layer = cfg.qkv_rows * H + H * cfg.heads * cfg.head_dim + 2 * cfg.inter * H + H * cfg.inter
+    linear_flops = 2.0 * m * per_layer * cfg.layers + 2.0 * batch * cfg.vocab * H
+    # causal attention: q.k and p.v over (pos + 1) keys for every row and head
+    attn_flops = 4.0 * batch * cfg.heads * cfg.head_dim * cfg.layers * sum(p + 1 for p in range(tokens))
+    del dec
+    torch.cuda.synchronize(dev)
+    return {"config": f"configs[3]: the decoder's prompt pass, batch {batch} x {tokens} random-id tokens (M = {m}): "
+                      "embedding, per layer rms_norm, qkv, RoPE + KV append, causal attention, o + residual, "
+                      "rms_norm, gate_up, SwiGLU, down + residual; final norm, LM head and argmax per sequence",
+            "ms_per_pass": ms, "tokens_per_s": world * m / (ms * 1e-3),
+            "tflops": (linear_flops + attn_flops) / (ms * 1e-3) / 1e12 * world,
+            "linear_gflop": linear_flops / 1e9, "attention_gflop": attn_flops / 1e9}
 
 
 def run_profile_decoder(args) -> None:
@@ -553,7 +619,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     ap.add_argument("--no-tp-mlp", action="store_true", help="skip the tensor-parallel MLP measurement")
     ap.add_argument("--no-decoder", action="store_true", help="skip the config-2 decoder tokens/s measurement")
-    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill (M = 4096) linears")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the config-3 prefill legs (M = 4096 linears, decoder prompt pass)")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="layer copies (28 = the benchmark; fewer only for small profiling captures)")
     ap.add_argument("--case", default=None,
@@ -860,6 +927,7 @@ def main() -> None:
         line["decoder"] = run_decoder(torch, dist, dev, rank, world)
     if not args.no_prefill:
         line["prefill"] = run_prefill(torch, dist, L, dev, stream, mats, rank, world)
+        line["decoder_prefill"] = run_decoder_prefill(torch, dist, dev, rank, world)
     if args.sweep and rank == 0:
         line["sweep"] = run_sweep(torch, L, dev, stream)
     if rank == 0:

@@ -255,6 +255,32 @@ int q8lin_rope_attention_decode_ex(const float* qkv, const int32_t* pos, const f
                                    float* out, uint32_t flags, q8lin_stream_t stream);
 /* x[0..n) += y[0..n). */
 int q8lin_add(float* x, const float* y, int64_t n, q8lin_stream_t stream);
+
+/*
+ * Prefill building blocks: `batch` sequences, each with t new rows at positions
+ * pos0 .. pos0 + t - 1 (pos0 a host value), run as one batched forward -- the prompt
+ * pass `self.base.forward(&input, ...)` with M = context of crates/voxcpm/src/
+ * model.rs:492-495 through transformer.rs:107-155 (offset = pos0).  The linears,
+ * norms, SwiGLU and residual adds of that pass are q8lin_forward / q8lin_rmsnorm /
+ * q8lin_swiglu / q8lin_add at M = batch * t.  Row r = s * t + i of sequence s, new row i.
+ * Both return Q8LIN_ERR_SHAPE when pos0 < 0 or pos0 + t > max_t (the reference's
+ * "Transformer context limit exceeded", transformer.rs:110-113).
+ *
+ * qkv[batch * t][(hq + 2 hkv) * d]: rotated q -> q_out[batch * t][hq][d]; rotated k and
+ * v -> k_cache / v_cache [batch][hkv][max_t][d] at rows pos0 + i (rotate(),
+ * transformer.rs:159-170; the cat-growth of :131-139 preallocated).
+ */
+int q8lin_rope_kv_rows(const float* qkv, int32_t batch, int64_t t, int32_t pos0, const float* cos_t,
+                       const float* sin_t, float* k_cache, float* v_cache, int32_t hq, int32_t hkv, int32_t d,
+                       int32_t max_t, float* q_out, q8lin_stream_t stream);
+/* Causal grouped attention of the new rows: out[batch * t][hq][d] = softmax(q K^T /
+ * sqrt(d)) V over cache rows [0, pos0 + i] of the row's sequence (attention.rs:28-98,
+ * causal mask :84-95), kv head = q head / (hq / hkv); d = 128.  The cache rows
+ * [0, pos0 + t) must be written (q8lin_rope_kv_rows for the new ones).  q, the caches
+ * and out 16-byte aligned.  No workspace. */
+int q8lin_attention_prefill(const float* q, const float* k_cache, const float* v_cache, int32_t batch, int64_t t,
+                            int32_t pos0, int32_t hq, int32_t hkv, int32_t d, int32_t max_t, float* out,
+                            q8lin_stream_t stream);
 size_t q8lin_argmax_workspace_size(void);
 /* *token = argmax(logits[0..n)) (lowest index on ties); if pos != NULL, *pos += 1.  The
  * workspace must be zero-filled once before first use. */

@@ -1,4 +1,4 @@
-"""CPU reference of one batch-1 decode step of the Q8_0 decoder.
+"""CPU reference of the Q8_0 decoder: one batch-1 decode step, and the prompt pass.
 
 TEST INFRASTRUCTURE ONLY (see q8_0_oracle.c): the checker for
 talechime_b200/decoder.py.  Restates crates/voxcpm/src/transformer.rs:107-155 (layer
@@ -73,4 +73,47 @@ class DecoderRef:
             d = oracle.matmul(oracle.swiglu(gu), np.asarray(lw["down"]), H)[0]
             x = (x + d).astype(np.float32)
         h = _rms_norm(x, np.asarray(w["output_norm"]), cfg.eps)
+        return oracle.matmul(h[None, :], np.asarray(w["output"]), cfg.vocab)[0]
+
+    def prefill(self, tokens, pos0: int) -> np.ndarray:
+        """Logits f32 [vocab] of the last of `tokens`, run as ONE forward of T = len(tokens)
+        rows at positions pos0 .. pos0 + T - 1 (the prompt pass of crates/voxcpm/src/
+        model.rs:492-495 through transformer.rs:107-155 with offset = pos0): every linear
+        takes all T rows at once (candle's QMatMul quantizes and dots each row on its
+        own), RoPE rotates row i at position pos0 + i, the cache grows by T rows, and row
+        i attends to cache rows [0, pos0 + i] (the causal mask of attention.rs:84-95
+        excludes key j when j > offset + i); the caller's next token comes from the last
+        row (the reference's norm -> head on x[:, t - 1])."""
+        cfg, w = self.cfg, self.w
+        H, D, Hq, Hk = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads
+        T = len(tokens)
+        if pos0 < 0 or pos0 + T > cfg.max_t:
+            raise ValueError("Transformer context limit exceeded")
+        scale = np.float32(1.0 / np.sqrt(float(D)))
+        x = np.stack([_dequant_row(np.asarray(w["token_embd"]), int(t), H) for t in tokens]).astype(np.float32)
+        for li in range(cfg.layers):
+            lw = w["layers"][li]
+            h = np.stack([_rms_norm(r, np.asarray(lw["attn_norm"]), cfg.eps) for r in x])
+            qkv = oracle.matmul(h, np.asarray(lw["qkv"]), cfg.qkv_rows)
+            q = np.empty((T, Hq, D), np.float32)
+            for i in range(T):
+                q[i] = self._rope(qkv[i, :Hq * D].reshape(Hq, D), pos0 + i)
+                self.k[li][:, pos0 + i] = self._rope(qkv[i, Hq * D:(Hq + Hk) * D].reshape(Hk, D), pos0 + i)
+                self.v[li][:, pos0 + i] = qkv[i, (Hq + Hk) * D:].reshape(Hk, D)
+            att = np.empty((T, Hq, D), np.float32)
+            for hh in range(Hq):
+                kh = hh // (Hq // Hk)
+                for i in range(T):
+                    n = pos0 + i + 1  # visible keys
+                    sc = (self.k[li][kh, :n] @ q[i, hh]).astype(np.float32) * scale
+                    e = np.exp((sc - sc.max()).astype(np.float32)).astype(np.float32)
+                    p = (e / e.sum(dtype=np.float32)).astype(np.float32)
+                    att[i, hh] = (p @ self.v[li][kh, :n]).astype(np.float32)
+            o = oracle.matmul(att.reshape(T, Hq * D), np.asarray(lw["o"]), H)
+            x = (x + o).astype(np.float32)
+            h = np.stack([_rms_norm(r, np.asarray(lw["ffn_norm"]), cfg.eps) for r in x])
+            gu = oracle.matmul(h, np.asarray(lw["gate_up"]), 2 * cfg.inter)
+            d = oracle.matmul(oracle.swiglu(gu), np.asarray(lw["down"]), H)
+            x = (x + d).astype(np.float32)
+        h = _rms_norm(x[T - 1], np.asarray(w["output_norm"]), cfg.eps)
         return oracle.matmul(h[None, :], np.asarray(w["output"]), cfg.vocab)[0]

@@ -95,6 +95,12 @@ SIGNATURES = {
                                                       ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_p,
                                                       ctypes.c_uint32, _c_p]),
     "q8lin_add": (ctypes.c_int, [_c_p, _c_p, _i64, _c_p]),
+    "q8lin_rope_kv_rows": (ctypes.c_int, [_c_p, ctypes.c_int32, _i64, ctypes.c_int32, _c_p, _c_p, _c_p, _c_p,
+                                          ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_p,
+                                          _c_p]),
+    "q8lin_attention_prefill": (ctypes.c_int, [_c_p, _c_p, _c_p, ctypes.c_int32, _i64, ctypes.c_int32,
+                                               ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_p,
+                                               _c_p]),
     "q8lin_peer_alloc": (ctypes.c_int, [ctypes.c_int, ctypes.c_size_t, ctypes.POINTER(_c_p), _c_p]),
     "q8lin_peer_open": (ctypes.c_int, [ctypes.c_int, _c_p, ctypes.POINTER(_c_p)]),
     "q8lin_peer_close": (ctypes.c_int, [ctypes.c_int, _c_p]),

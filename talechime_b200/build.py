@@ -20,7 +20,7 @@ LIB = os.path.join(PKG, "libq8lin.so")
 OBJDIR = os.path.join(PKG, "_build")
 
 SOURCES = ["abi.cu", "layout.cu", "gemv.cu", "gemm_simt.cu", "gemm_tc.cu", "noalloc.cu", "mlp.cu", "gemm_skinny.cu", "decoder.cu",
-           "step.cu", "gemv_mrow.cu", "gguf.cpp", "tp_mlp.cu", "gemm_mma.cu"]
+           "step.cu", "gemv_mrow.cu", "gguf.cpp", "tp_mlp.cu", "gemm_mma.cu", "prefill.cu"]
 HEADERS = ["common.cuh", "internal.h"]
 
 NVCC_FLAGS = [

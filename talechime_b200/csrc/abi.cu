@@ -705,6 +705,49 @@ int q8lin_rope_attention_decode_ex(const float* qkv, const int32_t* pos, const f
   return Q8LIN_OK;
 }
 
+// pos0 / t / batch / head counts of a prefill call (the context-limit check of
+// transformer.rs:110-113 included); 0 when they are valid.
+static int prefill_shape_fail(int32_t batch, int64_t t, int32_t pos0, int32_t hq, int32_t hkv, int32_t d,
+                              int32_t max_t, int max_d) {
+  if (hq <= 0 || hkv <= 0 || hq % hkv || d <= 0 || d % 2 || d > max_d || max_t <= 0 || hq + 2 * hkv > 65535)
+    return fail(Q8LIN_ERR_SHAPE, "prefill needs hq a positive multiple of hkv, a supported head width and max_t > 0");
+  if (batch <= 0 || batch > 65535 || t < 0) return fail(Q8LIN_ERR_SHAPE, "prefill needs 0 < batch <= 65535 and t >= 0");
+  if ((int64_t)batch * t > INT32_MAX) return fail(Q8LIN_ERR_SHAPE, "prefill needs batch * t < 2^31");
+  if (pos0 < 0 || (int64_t)pos0 + t > max_t) return fail(Q8LIN_ERR_SHAPE, "Transformer context limit exceeded");
+  return Q8LIN_OK;
+}
+
+int q8lin_rope_kv_rows(const float* qkv, int32_t batch, int64_t t, int32_t pos0, const float* cos_t,
+                       const float* sin_t, float* k_cache, float* v_cache, int32_t hq, int32_t hkv, int32_t d,
+                       int32_t max_t, float* q_out, q8lin_stream_t stream) {
+  if (int st = prefill_shape_fail(batch, t, pos0, hq, hkv, d, max_t, 1024)) return st;
+  if (!qkv || !cos_t || !sin_t || !k_cache || !v_cache || !q_out)
+    return fail(Q8LIN_ERR_INVALID_ARGUMENT, "rope pointers must be non-null device pointers");
+  if (t == 0) return Q8LIN_OK;
+  cudaError_t e = launch_rope_kv_rows(qkv, batch, (int)t, pos0, cos_t, sin_t, k_cache, v_cache, hq, hkv, d, max_t,
+                                      q_out, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope_kv_rows launch");
+  return Q8LIN_OK;
+}
+
+int q8lin_attention_prefill(const float* q, const float* k_cache, const float* v_cache, int32_t batch, int64_t t,
+                            int32_t pos0, int32_t hq, int32_t hkv, int32_t d, int32_t max_t, float* out,
+                            q8lin_stream_t stream) {
+  if (d != 128) return fail(Q8LIN_ERR_SHAPE, "attention_prefill supports head width 128");
+  if (int st = prefill_shape_fail(batch, t, pos0, hq, hkv, d, max_t, 128)) return st;
+  if (!q || !k_cache || !v_cache || !out)
+    return fail(Q8LIN_ERR_INVALID_ARGUMENT, "attention pointers must be non-null device pointers");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
+    return fail(Q8LIN_ERR_ALIGNMENT, "q, the caches and out must be 16-byte aligned");
+  if (t == 0) return Q8LIN_OK;
+  int device = 0;
+  cudaGetDevice(&device);
+  cudaError_t e = launch_attention_prefill(q, k_cache, v_cache, batch, (int)t, pos0, hq, hkv, max_t, out, device,
+                                           reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention_prefill launch");
+  return Q8LIN_OK;
+}
+
 int q8lin_add(float* x, const float* y, int64_t n, q8lin_stream_t stream) {
   if (n < 0) return fail(Q8LIN_ERR_SHAPE, "n must be non-negative");
   if (n == 0) return Q8LIN_OK;

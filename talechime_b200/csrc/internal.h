@@ -158,6 +158,14 @@ cudaError_t launch_rope_attention(const float* qkv, const int* pos, const float*
 cudaError_t read_attention_fault(unsigned int* flags, bool clear);  // bit 3
 cudaError_t launch_add(float* x, const float* y, int64_t n, cudaStream_t s);
 
+// Prefill kernels (prefill.cu): `batch` sequences of t rows at positions pos0 .. pos0+t-1
+// (host values, checked by the caller: pos0 >= 0, pos0 + t <= max_t); caches
+// [batch][hkv][max_t][d].
+cudaError_t launch_rope_kv_rows(const float* qkv, int batch, int t, int pos0, const float* cos_t, const float* sin_t,
+                                float* kc, float* vc, int hq, int hkv, int d, int max_t, float* q_out, cudaStream_t s);
+cudaError_t launch_attention_prefill(const float* q, const float* kc, const float* vc, int batch, int t, int pos0,
+                                     int hq, int hkv, int max_t, float* out, int device, cudaStream_t s);
+
 // Persistent decode-step kernel (step.cu).
 constexpr int kStepMaxK = 8192;
 enum StepOpKind { kStepOpGemv = 0, kStepOpAttention = 1, kStepOpEmbed = 2, kStepOpArgmax = 3 };

@@ -135,7 +135,12 @@ class Q8Decoder:
         return cls(cfg, weights, device=device, rope_factors=factors)
 
     def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | int | str = 0,
-                 rope_factors: Optional[np.ndarray] = None):
+                 rope_factors: Optional[np.ndarray] = None, batch: int = 1):
+        """`batch` sequences share the weights and the position; each has its own KV cache
+        (prefill() takes [batch, T] tokens); the decode step serves batch 1."""
+        if batch < 1:
+            raise ValueError("batch must be positive")
+        self.batch = int(batch)
         if cfg.head_dim != 128:
             raise _lib.Q8LinError(_lib.ERR_SHAPE, "the decode attention kernel takes head_dim 128")
         self.cfg = cfg
@@ -172,6 +177,8 @@ class Q8Decoder:
         self.cos = torch.from_numpy(cos).to(dev)
         self.sin = torch.from_numpy(sin).to(dev)
         kv_shape = (cfg.kv_heads, cfg.max_t, cfg.head_dim)
+        if self.batch > 1:
+            kv_shape = (self.batch,) + kv_shape
         self.k_cache = [torch.zeros(kv_shape, device=dev) for _ in range(cfg.layers)]
         self.v_cache = [torch.zeros(kv_shape, device=dev) for _ in range(cfg.layers)]
         f = lambda n: torch.zeros(n, device=dev)
@@ -208,6 +215,9 @@ class Q8Decoder:
         projection's activation quantization, the residual adds inside the o / down
         projections and RoPE + KV append inside the attention kernel (5 launches per
         layer); "unfused": 11 launches per layer, one per reference operation."""
+        if self.batch != 1:
+            raise ValueError("the decode step serves batch 1; this decoder holds "
+                             f"{self.batch} sequences (prefill only)")
         if mode == "persistent":
             check(_lib.lib().q8lin_step_run(self._persistent(), ctypes.c_void_p(_stream_ptr(self.device))))
         elif mode == "fused":
@@ -298,6 +308,72 @@ class Q8Decoder:
         self.lm_head.forward(self.h.view(1, H), out=self.logits.view(1, -1))
         check(L.q8lin_argmax(P(self.logits), cfg.vocab, P(self.argmax_ws), self.argmax_ws.numel(), P(self.token),
                              P(self.pos), s))
+
+    def prefill(self, tokens) -> torch.Tensor:
+        """Run a prompt as ONE batched forward: `tokens` [T] (batch 1) or [batch, T] ids at
+        positions pos .. pos + T - 1 of every sequence (crates/voxcpm/src/model.rs:492-495,
+        transformer.rs:107-155 with offset = pos): the linears at M = batch * T, RoPE and
+        the KV append per row (q8lin_rope_kv_rows), causal attention (q8lin_attention_
+        prefill), then the final norm, LM head and greedy pick on each sequence's last
+        row.  Returns the next token of each sequence (int32 [batch] on the device);
+        afterwards the caches hold the T new rows, pos has advanced by T, self.logits
+        holds the last row's logits (batch 1; self.prefill_logits [batch, vocab]) and,
+        for batch 1, self.token the next token -- the state T decode steps over the same
+        tokens leave.  Raises Q8LinError(ERR_SHAPE) past max_t, as the reference's
+        "Transformer context limit exceeded" (transformer.rs:110-113)."""
+        cfg, L, P = self.cfg, _lib.lib(), self._p
+        tok = torch.as_tensor(np.asarray(tokens.cpu() if isinstance(tokens, torch.Tensor) else tokens),
+                              dtype=torch.int32)
+        if tok.dim() == 1:
+            tok = tok.unsqueeze(0)
+        if tok.dim() != 2 or tok.shape[0] != self.batch:
+            raise _lib.Q8LinError(_lib.ERR_SHAPE, f"tokens must be [T] or [{self.batch}, T]; got {tuple(tok.shape)}")
+        B, T = tok.shape
+        pos0 = int(self.pos.item())
+        if T == 0:
+            raise _lib.Q8LinError(_lib.ERR_SHAPE, "prefill needs at least one token")
+        if pos0 + T > cfg.max_t:
+            raise _lib.Q8LinError(_lib.ERR_SHAPE, "Transformer context limit exceeded")
+        dev, H, M = self.device, cfg.hidden, B * T
+        hd = cfg.heads * cfg.head_dim
+        s = ctypes.c_void_p(_stream_ptr(dev))
+        e = lambda *shape: torch.empty(shape, dtype=torch.float32, device=dev)
+        tok_d = tok.reshape(-1).to(dev)
+        x, hn, qkv, q, att, t1 = e(M, H), e(M, H), e(M, cfg.qkv_rows), e(M, hd), e(M, hd), e(M, H)
+        gu, hm = e(M, 2 * cfg.inter), e(M, cfg.inter)
+        check(L.q8lin_embed_rows(self.embed.handle, P(tok_d), M, P(x), s))
+        for li, w in enumerate(self.layers):
+            check(L.q8lin_rmsnorm(P(x), P(w["attn_norm"]), M, H, cfg.eps, P(hn), s))
+            w["qkv"].forward(hn, out=qkv)
+            check(L.q8lin_rope_kv_rows(P(qkv), B, T, pos0, P(self.cos), P(self.sin), P(self.k_cache[li]),
+                                       P(self.v_cache[li]), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.max_t,
+                                       P(q), s))
+            check(L.q8lin_attention_prefill(P(q), P(self.k_cache[li]), P(self.v_cache[li]), B, T, pos0, cfg.heads,
+                                            cfg.kv_heads, cfg.head_dim, cfg.max_t, P(att), s))
+            w["o"].forward(att, out=t1)
+            check(L.q8lin_add(P(x), P(t1), M * H, s))
+            check(L.q8lin_rmsnorm(P(x), P(w["ffn_norm"]), M, H, cfg.eps, P(hn), s))
+            w["gate_up"].forward(hn, out=gu)
+            check(L.q8lin_swiglu(P(gu), M, cfg.inter, P(hm), s))
+            w["down"].forward(hm, out=t1)
+            check(L.q8lin_add(P(x), P(t1), M * H, s))
+        last = e(B, H)
+        for b in range(B):  # each sequence's last row
+            check(L.q8lin_rmsnorm(ctypes.c_void_p(x.data_ptr() + ((b * T + T - 1) * H) * 4), P(self.out_norm), 1, H,
+                                  cfg.eps, ctypes.c_void_p(last.data_ptr() + b * H * 4), s))
+        logits = e(B, cfg.vocab)
+        self.lm_head.forward(last, out=logits)
+        nxt = torch.empty(B, dtype=torch.int32, device=dev)
+        for b in range(B):
+            check(L.q8lin_argmax(ctypes.c_void_p(logits.data_ptr() + b * cfg.vocab * 4), cfg.vocab,
+                                 P(self.argmax_ws), self.argmax_ws.numel(), ctypes.c_void_p(nxt.data_ptr() + 4 * b),
+                                 None, s))
+        self.pos.fill_(pos0 + T)
+        self.prefill_logits = logits
+        if B == 1:
+            self.logits.copy_(logits[0])
+            self.token.copy_(nxt)
+        return nxt
 
     def launches_per_step(self, mode: str = "fused") -> int:
         if mode == "persistent":

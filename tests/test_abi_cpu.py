@@ -71,6 +71,30 @@ def test_quantize_rows_shape_checks(lib):
     assert lib.q8lin_quantize_rows(None, 2, 64, None, None, None) == 1
 
 
+def test_prefill_entry_points_check_arguments_before_touching_cuda(lib):
+    """The prompt-pass kernels refuse a context past max_t (the reference's "Transformer
+    context limit exceeded", transformer.rs:110-113), bad head shapes, null and
+    misaligned pointers, all before any CUDA call; t = 0 is a no-op."""
+    P = ctypes.c_void_p
+    good, odd = P(4096), P(4100)
+    rope = lambda b, t, p0, hq=4, hkv=2, d=128, mt=16, ptr=good: lib.q8lin_rope_kv_rows(
+        ptr, b, t, p0, ptr, ptr, ptr, ptr, hq, hkv, d, mt, ptr, None)
+    attn = lambda b, t, p0, hq=4, hkv=2, d=128, mt=16, ptr=good: lib.q8lin_attention_prefill(
+        ptr, ptr, ptr, b, t, p0, hq, hkv, d, mt, ptr, None)
+    for fn in (rope, attn):
+        assert fn(1, 10, 7) == 2  # 7 + 10 > 16
+        assert b"context limit" in lib.q8lin_last_error()
+        assert fn(1, 4, -1) == 2
+        assert fn(0, 4, 0) == 2
+        assert fn(1, -1, 0) == 2
+        assert fn(1, 4, 0, hq=3) == 2  # not a multiple of hkv
+        assert fn(1, 4, 0, ptr=None) == 1
+        assert fn(1, 0, 16) == 0  # nothing to do, at the limit
+    assert attn(1, 4, 0, d=64) == 2
+    assert attn(1, 4, 0, ptr=odd) == 3
+    assert lib.q8lin_status_string(3) == b"Q8LIN_ERR_ALIGNMENT"
+
+
 def test_destroy_null_is_noop(lib):
     assert lib.q8lin_weight_destroy(None) == 0
 
