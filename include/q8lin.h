@@ -255,6 +255,11 @@ int q8lin_rope_attention_decode_ex(const float* qkv, const int32_t* pos, const f
                                    float* out, uint32_t flags, q8lin_stream_t stream);
 /* x[0..n) += y[0..n). */
 int q8lin_add(float* x, const float* y, int64_t n, q8lin_stream_t stream);
+/* x[m][n] += y[m][n], then h[m][n] = x / sqrt(sum(x^2)/n + eps) * weight: the residual add
+ * and the rms_norm after it (crates/voxcpm/src/transformer.rs:146-147, and :116-117 of
+ * the next layer) in one pass over the rows; x and h must not overlap. */
+int q8lin_add_rmsnorm(float* x, const float* y, const float* weight, int64_t m, int64_t n, float eps, float* h,
+                      q8lin_stream_t stream);
 
 /*
  * Prefill building blocks: `batch` sequences, each with t new rows at positions

@@ -95,6 +95,7 @@ SIGNATURES = {
                                                       ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_p,
                                                       ctypes.c_uint32, _c_p]),
     "q8lin_add": (ctypes.c_int, [_c_p, _c_p, _i64, _c_p]),
+    "q8lin_add_rmsnorm": (ctypes.c_int, [_c_p, _c_p, _c_p, _i64, _i64, ctypes.c_float, _c_p, _c_p]),
     "q8lin_rope_kv_rows": (ctypes.c_int, [_c_p, ctypes.c_int32, _i64, ctypes.c_int32, _c_p, _c_p, _c_p, _c_p,
                                           ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _c_p,
                                           _c_p]),

@@ -748,6 +748,16 @@ int q8lin_attention_prefill(const float* q, const float* k_cache, const float* v
   return Q8LIN_OK;
 }
 
+int q8lin_add_rmsnorm(float* x, const float* y, const float* weight, int64_t m, int64_t n, float eps, float* h,
+                      q8lin_stream_t stream) {
+  if (m < 0 || n <= 0 || m > INT32_MAX) return fail(Q8LIN_ERR_SHAPE, "add_rmsnorm needs 0 <= m < 2^31 and n > 0");
+  if (m == 0) return Q8LIN_OK;
+  if (!x || !y || !weight || !h) return fail(Q8LIN_ERR_INVALID_ARGUMENT, "add_rmsnorm pointers must be non-null");
+  cudaError_t e = launch_add_rmsnorm(x, y, weight, eps, m, n, h, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "add_rmsnorm launch");
+  return Q8LIN_OK;
+}
+
 int q8lin_add(float* x, const float* y, int64_t n, q8lin_stream_t stream) {
   if (n < 0) return fail(Q8LIN_ERR_SHAPE, "n must be non-negative");
   if (n == 0) return Q8LIN_OK;

@@ -163,6 +163,10 @@ cudaError_t launch_add(float* x, const float* y, int64_t n, cudaStream_t s);
 // [batch][hkv][max_t][d].
 cudaError_t launch_rope_kv_rows(const float* qkv, int batch, int t, int pos0, const float* cos_t, const float* sin_t,
                                 float* kc, float* vc, int hq, int hkv, int d, int max_t, float* q_out, cudaStream_t s);
+// x[m][n] += y; h = rms_norm(x) * w (one kernel where n % 4 == 0, n <= 8192 and the rows
+// are 16-byte aligned; else the add and rmsnorm kernels).
+cudaError_t launch_add_rmsnorm(float* x, const float* y, const float* w, float eps, int64_t m, int64_t n, float* h,
+                               cudaStream_t s);
 cudaError_t launch_attention_prefill(const float* q, const float* kc, const float* vc, int batch, int t, int pos0,
                                      int hq, int hkv, int max_t, float* out, int device, cudaStream_t s);
 

@@ -55,6 +55,100 @@ __global__ void rope_kv_rows_kernel(const float* __restrict__ qkv, int T, int po
   }
 }
 
+// The same rotation with float4 pieces, one CTA per row (d % 8 == 0, 16-byte aligned
+// rows): a thread rotates four dimensions of each half of a head at once, with the
+// per-element products and sums of the scalar kernel, so the results are identical.
+__global__ void __launch_bounds__(256)
+rope_kv_rows_vec_kernel(const float* __restrict__ qkv, int T, int pos0, const float* __restrict__ cos_t,
+                        const float* __restrict__ sin_t, float* __restrict__ kc, float* __restrict__ vc, int Hq,
+                        int Hkv, int D, int max_t, float* __restrict__ q_out) {
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
+  pdl_wait();
+  const int row = blockIdx.x;
+  const int b = row / T, t = row - b * T;
+  const int pos = pos0 + t;
+  if (pos < 0 || pos >= max_t) return;
+  const int half = D / 2, h4 = half / 4, d4 = D / 4;
+  const float4* xr = reinterpret_cast<const float4*>(qkv + (size_t)row * (Hq + 2 * Hkv) * D);
+  const float4* c4 = reinterpret_cast<const float4*>(cos_t + (size_t)pos * half);
+  const float4* s4 = reinterpret_cast<const float4*>(sin_t + (size_t)pos * half);
+  const int nrot = (Hq + Hkv) * h4;
+  for (int it = threadIdx.x; it < nrot; it += blockDim.x) {
+    const int head = it / h4, j = it - head * h4;
+    const float4 a = xr[head * d4 + j], o = xr[head * d4 + h4 + j];
+    const float4 c = __ldg(c4 + j), sn = __ldg(s4 + j);
+    // first half x*cos + second*(-sin); second half x*cos + first*sin
+    const float4 lo = make_float4(__fadd_rn(__fmul_rn(a.x, c.x), __fmul_rn(o.x, -sn.x)),
+                                  __fadd_rn(__fmul_rn(a.y, c.y), __fmul_rn(o.y, -sn.y)),
+                                  __fadd_rn(__fmul_rn(a.z, c.z), __fmul_rn(o.z, -sn.z)),
+                                  __fadd_rn(__fmul_rn(a.w, c.w), __fmul_rn(o.w, -sn.w)));
+    const float4 hi = make_float4(__fadd_rn(__fmul_rn(o.x, c.x), __fmul_rn(a.x, sn.x)),
+                                  __fadd_rn(__fmul_rn(o.y, c.y), __fmul_rn(a.y, sn.y)),
+                                  __fadd_rn(__fmul_rn(o.z, c.z), __fmul_rn(a.z, sn.z)),
+                                  __fadd_rn(__fmul_rn(o.w, c.w), __fmul_rn(a.w, sn.w)));
+    float4* dst = head < Hq ? reinterpret_cast<float4*>(q_out + ((size_t)row * Hq + head) * D)
+                            : reinterpret_cast<float4*>(kc + (((size_t)b * Hkv + (head - Hq)) * max_t + pos) * D);
+    dst[j] = lo;
+    dst[h4 + j] = hi;
+  }
+  const int nv = Hkv * d4;
+  for (int it = threadIdx.x; it < nv; it += blockDim.x) {
+    const int hv = it / d4, j = it - hv * d4;
+    reinterpret_cast<float4*>(vc + (((size_t)b * Hkv + hv) * max_t + pos) * D)[j] = xr[(Hq + Hkv + hv) * d4 + j];
+  }
+}
+
+// x[r] += y[r]; h[r] = x[r] / sqrt(sum(x[r]^2) / n + eps) * w  (the residual add and the
+// rms_norm that follows it, transformer.rs:146-147 and :107-117 of the next layer), one
+// CTA of 256 threads per row, the row held in registers (n % 4 == 0, n <= 8192, 16-byte
+// aligned rows); sum of squares per thread, then warps, then the 8 warp sums in order.
+constexpr int kArThreads = 256;
+constexpr int kArMaxN = 8192;
+__global__ void __launch_bounds__(kArThreads)
+add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ w, float eps, int n,
+                   float* __restrict__ h) {
+  constexpr int kV = kArMaxN / 4 / kArThreads;
+  __shared__ float red[kArThreads / 32];
+  pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
+  pdl_wait();
+  float4* xr = reinterpret_cast<float4*>(x + (size_t)blockIdx.x * n);
+  const float4* yr = reinterpret_cast<const float4*>(y + (size_t)blockIdx.x * n);
+  float4* hr = reinterpret_cast<float4*>(h + (size_t)blockIdx.x * n);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const int n4 = n / 4;
+  float4 v[kV];
+  float sq = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kV; ++k) {
+    const int i = threadIdx.x + k * kArThreads;
+    if (i < n4) {
+      const float4 a = xr[i], bb = yr[i];
+      v[k] = make_float4(__fadd_rn(a.x, bb.x), __fadd_rn(a.y, bb.y), __fadd_rn(a.z, bb.z), __fadd_rn(a.w, bb.w));
+      xr[i] = v[k];
+      sq = __fadd_rn(sq, __fmul_rn(v[k].x, v[k].x));
+      sq = __fadd_rn(sq, __fmul_rn(v[k].y, v[k].y));
+      sq = __fadd_rn(sq, __fmul_rn(v[k].z, v[k].z));
+      sq = __fadd_rn(sq, __fmul_rn(v[k].w, v[k].w));
+    }
+  }
+  sq = warp_sum(sq);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  float total = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kArThreads / 32; ++i) total = __fadd_rn(total, red[i]);
+  const float m = __fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)n), eps));
+#pragma unroll
+  for (int k = 0; k < kV; ++k) {
+    const int i = threadIdx.x + k * kArThreads;
+    if (i < n4) {
+      const float4 wv = __ldg(w4 + i);
+      hr[i] = make_float4(__fmul_rn(__fdiv_rn(v[k].x, m), wv.x), __fmul_rn(__fdiv_rn(v[k].y, m), wv.y),
+                          __fmul_rn(__fdiv_rn(v[k].z, m), wv.z), __fmul_rn(__fdiv_rn(v[k].w, m), wv.w));
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------
 // attention_prefill: grid (ceil(T / 64), Hq, B), 256 threads; one CTA = 64 query rows
 // of one head of one sequence, flash-style over 64-key tiles of the cache:
@@ -267,8 +361,26 @@ cudaLaunchConfig_t pf_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t s, cu
 cudaError_t launch_rope_kv_rows(const float* qkv, int batch, int t, int pos0, const float* cos_t, const float* sin_t,
                                 float* kc, float* vc, int hq, int hkv, int d, int max_t, float* q_out, cudaStream_t s) {
   cudaLaunchAttribute attr[1];
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (d % 8 == 0 && a16(qkv) && a16(cos_t) && a16(sin_t) && a16(kc) && a16(vc) && a16(q_out)) {
+    cudaLaunchConfig_t cfg = pf_cfg(dim3((unsigned)(batch * t)), dim3(256), 0, s, attr);
+    return cudaLaunchKernelEx(&cfg, rope_kv_rows_vec_kernel, qkv, t, pos0, cos_t, sin_t, kc, vc, hq, hkv, d, max_t,
+                              q_out);
+  }
   cudaLaunchConfig_t cfg = pf_cfg(dim3((unsigned)(batch * t), (unsigned)(hq + 2 * hkv)), dim3((unsigned)d), 0, s, attr);
   return cudaLaunchKernelEx(&cfg, rope_kv_rows_kernel, qkv, t, pos0, cos_t, sin_t, kc, vc, hq, hkv, d, max_t, q_out);
+}
+
+cudaError_t launch_add_rmsnorm(float* x, const float* y, const float* w, float eps, int64_t m, int64_t n, float* h,
+                               cudaStream_t s) {
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (n % 4 == 0 && n <= kArMaxN && a16(x) && a16(y) && a16(w) && a16(h)) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pf_cfg(dim3((unsigned)m), dim3(kArThreads), 0, s, attr);
+    return cudaLaunchKernelEx(&cfg, add_rmsnorm_kernel, x, y, w, eps, (int)n, h);
+  }
+  cudaError_t e = launch_add(x, y, m * n, s);
+  return e != cudaSuccess ? e : launch_rmsnorm(x, w, eps, m, n, h, s);
 }
 
 cudaError_t launch_attention_prefill(const float* q, const float* kc, const float* vc, int batch, int t, int pos0,

@@ -314,8 +314,8 @@ class Q8Decoder:
         positions pos .. pos + T - 1 of every sequence (crates/voxcpm/src/model.rs:492-495,
         transformer.rs:107-155 with offset = pos): the linears at M = batch * T, RoPE and
         the KV append per row (q8lin_rope_kv_rows), causal attention (q8lin_attention_
-        prefill), then the final norm, LM head and greedy pick on each sequence's last
-        row.  Returns the next token of each sequence (int32 [batch] on the device);
+        prefill), each residual add fused with the norm after it (q8lin_add_rmsnorm), then
+        the final norm, LM head and greedy pick on each sequence's last row.  Returns the next token of each sequence (int32 [batch] on the device);
         afterwards the caches hold the T new rows, pos has advanced by T, self.logits
         holds the last row's logits (batch 1; self.prefill_logits [batch, vocab]) and,
         for batch 1, self.token the next token -- the state T decode steps over the same
@@ -342,8 +342,8 @@ class Q8Decoder:
         x, hn, qkv, q, att, t1 = e(M, H), e(M, H), e(M, cfg.qkv_rows), e(M, hd), e(M, hd), e(M, H)
         gu, hm = e(M, 2 * cfg.inter), e(M, cfg.inter)
         check(L.q8lin_embed_rows(self.embed.handle, P(tok_d), M, P(x), s))
+        check(L.q8lin_rmsnorm(P(x), P(self.layers[0]["attn_norm"]), M, H, cfg.eps, P(hn), s))
         for li, w in enumerate(self.layers):
-            check(L.q8lin_rmsnorm(P(x), P(w["attn_norm"]), M, H, cfg.eps, P(hn), s))
             w["qkv"].forward(hn, out=qkv)
             check(L.q8lin_rope_kv_rows(P(qkv), B, T, pos0, P(self.cos), P(self.sin), P(self.k_cache[li]),
                                        P(self.v_cache[li]), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.max_t,
@@ -351,12 +351,15 @@ class Q8Decoder:
             check(L.q8lin_attention_prefill(P(q), P(self.k_cache[li]), P(self.v_cache[li]), B, T, pos0, cfg.heads,
                                             cfg.kv_heads, cfg.head_dim, cfg.max_t, P(att), s))
             w["o"].forward(att, out=t1)
-            check(L.q8lin_add(P(x), P(t1), M * H, s))
-            check(L.q8lin_rmsnorm(P(x), P(w["ffn_norm"]), M, H, cfg.eps, P(hn), s))
+            # residual add + the norm after it, one pass: x += o(att); hn = ffn_norm(x)
+            check(L.q8lin_add_rmsnorm(P(x), P(t1), P(w["ffn_norm"]), M, H, cfg.eps, P(hn), s))
             w["gate_up"].forward(hn, out=gu)
             check(L.q8lin_swiglu(P(gu), M, cfg.inter, P(hm), s))
             w["down"].forward(hm, out=t1)
-            check(L.q8lin_add(P(x), P(t1), M * H, s))
+            if li + 1 < len(self.layers):  # x += down(h); hn = next layer's attn_norm(x)
+                check(L.q8lin_add_rmsnorm(P(x), P(t1), P(self.layers[li + 1]["attn_norm"]), M, H, cfg.eps, P(hn), s))
+            else:
+                check(L.q8lin_add(P(x), P(t1), M * H, s))
         last = e(B, H)
         for b in range(B):  # each sequence's last row
             check(L.q8lin_rmsnorm(ctypes.c_void_p(x.data_ptr() + ((b * T + T - 1) * H) * 4), P(self.out_norm), 1, H,

@@ -38,11 +38,13 @@ def _rope_np(x, pos, cos, sin):
     return ((x * c).astype(np.float32) + (sw * s).astype(np.float32)).astype(np.float32)
 
 
-def test_rope_kv_rows_is_the_reference_rotation(cuda_device):
+@pytest.mark.parametrize("D", [128, 100], ids=["float4_kernel", "scalar_kernel"])
+def test_rope_kv_rows_is_the_reference_rotation(cuda_device, D):
     """Every row rotated at its own position (bit-exact), k and v appended at rows
-    pos0 .. pos0 + T - 1 of their sequence's cache, every other cache row untouched."""
-    B, T, pos0, hq, hkv, D, max_t = 2, 5, 3, 4, 2, 128, 16
-    cfg = DecoderConfig(hidden=256, layers=1, heads=hq, kv_heads=hkv, inter=256, vocab=8, max_t=max_t)
+    pos0 .. pos0 + T - 1 of their sequence's cache, every other cache row untouched
+    (D = 128 takes the float4 kernel, D = 100 the scalar one)."""
+    B, T, pos0, hq, hkv, max_t = 2, 5, 3, 4, 2, 16
+    cfg = DecoderConfig(hidden=256, layers=1, heads=hq, kv_heads=hkv, head_dim=D, inter=256, vocab=8, max_t=max_t)
     cos, sin = rope_tables(cfg)
     rng = np.random.default_rng(3)
     qkv = rng.standard_normal((B * T, (hq + 2 * hkv) * D), dtype=np.float32)
@@ -68,6 +70,25 @@ def test_rope_kv_rows_is_the_reference_rotation(cuda_device):
     untouched = np.ones(max_t, bool)
     untouched[pos0:pos0 + T] = False
     assert np.all(kc[:, :, untouched] == 7.0) and np.all(vc[:, :, untouched] == -7.0)
+
+
+@pytest.mark.parametrize("m,n", [(3, 2048), (5, 6144), (2, 100)], ids=["hidden", "inter", "unaligned_width"])
+def test_add_rmsnorm_is_add_then_rmsnorm(cuda_device, m, n):
+    """x += y; h = x / sqrt(sum(x^2)/n + eps) * w: the sum exact per element (bit-exact x),
+    h against float64 within f32 summation-order tolerance (n = 100 takes the add and
+    rmsnorm kernels)."""
+    rng = np.random.default_rng(m + n)
+    x, y = rng.standard_normal((m, n), dtype=np.float32), rng.standard_normal((m, n), dtype=np.float32)
+    w = rng.uniform(0.5, 1.5, n).astype(np.float32)
+    dev = cuda_device
+    xd, yd, wd = (torch.from_numpy(a).to(dev) for a in (x, y, w))
+    hd = torch.empty((m, n), device=dev)
+    _lib.check(_lib.lib().q8lin_add_rmsnorm(_p(xd), _p(yd), _p(wd), m, n, 1e-5, _p(hd), _s()))
+    xs = (x + y).astype(np.float32)
+    assert np.array_equal(xd.cpu().numpy(), xs)
+    x64 = xs.astype(np.float64)
+    ref = x64 / np.sqrt((x64 * x64).sum(1, keepdims=True) / n + 1e-5) * w
+    np.testing.assert_allclose(hd.cpu().numpy(), ref, rtol=2e-6, atol=1e-6)
 
 
 def _attention_np(q, kc, vc, T, pos0, hq, hkv):
