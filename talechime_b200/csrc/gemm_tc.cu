@@ -44,6 +44,8 @@
 // reads with q8lin_fault_status and makes the CTA drain and return.
 #include <cuda.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -520,6 +522,399 @@ __global__ void quantize_rows_f16t_kernel(const float* __restrict__ x, int M, in
   pdl_launch_dependents();
 }
 
+// ---------------------------------------------------------------------------------
+// Exact-halves variant (gemm_q8_0_split_kernel): no per-block rescale inside the loop.
+//
+// Every dequantized Q8_0 value v = q * d (q int8, d f16) has at most 8 + 11 significant
+// bits, so after a power-of-two scale 2^e it is EXACTLY hi + lo with hi = f16(v 2^e) and
+// lo = f16(v 2^e - hi) -- as long as both halves stay normal f16 numbers, which the scale
+// ensures for every value within 2^-25 of the row's largest (smaller ones are off by at
+// most 2^-25 of that largest, far below f32 rounding of the sums).  Then
+//   y[m][n] = sum_k x[m][k] w[n][k] = 2^-(ea[m] + eb[n]) sum_k (xh + xl)(wh + wl)
+// and sum_k (xh wh + xh wl + xl wh) differs from the exact sum only by the xl wl terms
+// (each below 2^-22 of its product) and the tensor cores' f32 accumulation.  So one
+// 128 x 128 tile accumulates over all of K in TMEM with three kind::f16 MMAs per 16 K
+// values, and the epilogue runs once per chunk of `chunk_stages` stages (0: the whole K
+// range) instead of once per 32-value block.
+//   * activations: quantize_rows_split_kernel quantizes each row with candle's Q8_0 rules,
+//     picks ea[m] from the row's largest block scale and writes the hi and lo planes
+//     (f16 [M][K] each) and 2^-ea[m];
+//   * weights: the converter warps widen the int8 tile, multiply by the block scale and
+//     the row's 2^eb[n] (exact in f32) and write the hi and lo f16 tiles (128B-swizzled,
+//     K-major) that the MMAs read;
+//   * epilogue: y = chunk sums (f32, in chunk order) * 2^-ea[m] * 2^-eb[n] (exact).
+// Rings: TMA (kSpStages): A hi + A lo + B int8; converted (kSpBSlots): B hi + B lo.
+constexpr int kSpStages = 3;
+constexpr int kSpBSlots = 3;
+constexpr uint32_t kSpTmemCols = 2 * kBN;  // two chunk accumulators of kBN columns
+
+struct SpSmem {
+  alignas(1024) uint8_t a[kSpStages][2][kAStageBytes];  // [hi, lo] f16 tiles, swizzled
+  alignas(1024) uint8_t b[kSpBSlots][2][kBStageBytes];  // [hi, lo] f16 tiles, swizzled
+  alignas(128) uint8_t b8[kSpStages][kB8StageBytes];
+  alignas(16) float col_scale[kBN];  // 2^-eb of each weight row of the tile
+  alignas(8) uint64_t full[kSpStages];
+  alignas(8) uint64_t consumed[kSpStages];
+  alignas(8) uint64_t bfull[kSpBSlots];
+  alignas(8) uint64_t acc_full[2];
+  alignas(8) uint64_t acc_empty[2];
+  alignas(8) uint64_t scales_ready;
+  alignas(8) uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// 2^e for |e| <= 126 (exact).
+__device__ __forceinline__ float exp2i(int e) { return __int_as_float((127 + e) << 23); }
+
+// Scale exponent of a row whose values are q * d with |q| <= 128 and |d| <= dmax:
+// 128 * dmax * 2^e < 2^15, so hi halves stay below the f16 maximum.
+__device__ __forceinline__ int split_exponent(float dmax) {
+  if (!(dmax > 0.0f)) return 0;
+  int e;
+  frexpf(dmax, &e);  // dmax = f * 2^e, 0.5 <= f < 1
+  return 8 - e;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// The same halves in f16x2 arithmetic (converter warps): q as exact f16 integers,
+// hi = f16(q * s) (one rounding of the exact product) and lo = fma(q, s, -hi): the fused
+// f16 FMA forms q * s - hi exactly and that remainder fits an f16, so both halves equal
+// the f32 route's bit for bit.  s = d * 2^e as an f16 (exact while it stays normal; a
+// block whose scale is 2^-14 below f16's range is 2^-29 below the row's largest).
+__device__ __forceinline__ void split8_h(uint32_t w0, uint32_t w1, __half2 s2, uint4& hi, uint4& lo) {
+  const uint2 a = i8x4_to_f16x4(w0), b = i8x4_to_f16x4(w1);
+  const uint32_t q[4] = {a.x, a.y, b.x, b.y};
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 qv = *reinterpret_cast<const __half2*>(&q[i]);
+    const __half2 hv = __hmul2(qv, s2);
+    const __half2 lv = __hfma2(qv, s2, __hneg2(hv));
+    h[i] = *reinterpret_cast<const uint32_t*>(&hv);
+    l[i] = *reinterpret_cast<const uint32_t*>(&lv);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Eight products q * s (q from two int8 words, s = d * 2^e) -> hi and lo f16x8.
+__device__ __forceinline__ void split8(uint32_t w0, uint32_t w1, float s, uint4& hi, uint4& lo) {
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[i] = __fmul_rn((float)(int8_t)(w0 >> (8 * i)), s);
+    v[4 + i] = __fmul_rn((float)(int8_t)(w1 >> (8 * i)), s);
+  }
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    h[i] = pack_h2(v[2 * i], v[2 * i + 1]);
+    const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&h[i]));
+    l[i] = pack_h2(__fsub_rn(v[2 * i], hf.x), __fsub_rn(v[2 * i + 1], hf.y));
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_q8_0_split_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
+                       const __grid_constant__ CUtensorMap map_b, const uint8_t* __restrict__ W, int64_t S, int N,
+                       int K, const float* __restrict__ row_scale, float* __restrict__ y, int M, int splits,
+                       float* __restrict__ part, int chunk_stages, uint64_t wait_ns) {
+  extern __shared__ uint8_t smem_raw[];
+  SpSmem& sm = *reinterpret_cast<SpSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kBN;
+  const int m0 = blockIdx.y * kBM;
+  const int nb = K >> 5;
+  const int nstages_all = (K + kBK - 1) / kBK;
+  const int ngroups_all = (nstages_all + kGroupStages - 1) / kGroupStages;
+  const int split = blockIdx.z;
+  const int gbeg = (int)(((int64_t)ngroups_all * split) / splits);
+  const int gend = (int)(((int64_t)ngroups_all * (split + 1)) / splits);
+  const int sbeg = gbeg * kGroupStages;
+  const int nstages = min(gend * kGroupStages, nstages_all) - sbeg;
+  const int cs = (chunk_stages > 0 && chunk_stages < nstages) ? chunk_stages : max(nstages, 1);
+  const int nchunks = (nstages + cs - 1) / cs;
+  volatile int* abort = &sm.abort;
+
+  if (threadIdx.x == 0) {
+    s_wait_ns = wait_ns;
+    for (int i = 0; i < kSpStages; ++i) {
+      mbar_init(&sm.full[i], 3);  // A hi, A lo, B int8: each from its own lane
+      mbar_init(&sm.consumed[i], 1);
+    }
+    for (int i = 0; i < kSpBSlots; ++i) mbar_init(&sm.bfull[i], kConvWarps);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.acc_full[i], 1);
+      mbar_init(&sm.acc_empty[i], kEpiWarps);
+    }
+    mbar_init(&sm.scales_ready, kConvWarps);
+    mbar_init(&sm.mma_done, 1);
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&sm.tmem_base)),
+                 "r"(kSpTmemCols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (three lanes per stage, rotating) ----------------
+    constexpr int kIssueTriples = 4;
+    pdl_wait();  // the activation planes come from the upstream quantize kernel
+    int issued = 0;
+    for (int s = 0; s < nstages; ++s) {
+      const int st = s % kSpStages;
+      if (s >= kSpStages && !warp_wait(&sm.consumed[st], ((s / kSpStages) - 1) & 1, abort)) break;
+      const int gs = sbeg + s;
+      const int l0 = 3 * (s % kIssueTriples);
+      if (lane == l0) {
+        mbar_expect_tx(&sm.full[st], kAStageBytes);
+        tma_load_2d(sm.a[st][0], &map_ahi, gs * kBK, m0, &sm.full[st]);
+      } else if (lane == l0 + 1) {
+        mbar_expect_tx(&sm.full[st], kAStageBytes);
+        tma_load_2d(sm.a[st][1], &map_alo, gs * kBK, m0, &sm.full[st]);
+      } else if (lane == l0 + 2) {
+        mbar_expect_tx(&sm.full[st], kB8StageBytes);
+        tma_load_2d(sm.b8[st], &map_b, gs * kBK, n0, &sm.full[st]);
+      }
+      issued = s + 1;
+    }
+    if (lane == 0) {
+      for (int s = (issued > kSpStages ? issued - kSpStages : 0); s < issued; ++s)
+        mbar_drain(&sm.full[s % kSpStages], (s / kSpStages) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issue: 3 MMAs per 16 K into the chunk's accumulator ----------------
+    for (int s = 0; s < nstages; ++s) {
+      const int st = s % kSpStages, bs = s % kSpBSlots;
+      const int c = s / cs, buf = c & 1;
+      const bool first = (s % cs) == 0;
+      if (!warp_wait(&sm.full[st], (s / kSpStages) & 1, abort)) break;
+      if (!warp_wait(&sm.bfull[bs], (s / kSpBSlots) & 1, abort)) break;
+      if (first && c >= 2 && !warp_wait(&sm.acc_empty[buf], ((c >> 1) - 1) & 1, abort)) break;
+      tc_fence_after();
+      const uint64_t ah = umma_desc_sw128(sm.a[st][0]), al = umma_desc_sw128(sm.a[st][1]);
+      const uint64_t bh = umma_desc_sw128(sm.b[bs][0]), bl = umma_desc_sw128(sm.b[bs][1]);
+      const uint32_t d = tmem + (uint32_t)buf * kBN;
+      // a stage holding one block (odd nb, last stage) has zero K values 32..63 (TMA
+      // fill and zero weights): their MMAs are skipped
+      const int kk_end = (2 * (sbeg + s) + 1 < nb) ? 4 : 2;
+      for (int kk = 0; kk < kk_end; ++kk) {
+        const uint64_t off = (uint64_t)(kk * 2);  // 32 B of a 128 B swizzled row per 16 K
+        umma_f16(d, ah + off, bh + off, (first && kk == 0) ? 0u : 1u);
+        umma_f16(d, ah + off, bl + off, 1u);
+        umma_f16(d, al + off, bh + off, 1u);
+      }
+      umma_commit(&sm.consumed[st]);
+      if ((s + 1) % cs == 0 || s + 1 == nstages) umma_commit(&sm.acc_full[buf]);
+    }
+    umma_commit(&sm.mma_done);
+    __all_sync(0xffffffffu, mbar_drain(&sm.mma_done, 0));
+  } else if (warp < kEpiWarp0) {
+    // ---------------- weight conversion: thread ct owns weight row n0 + ct ----------------
+    const int ct = threadIdx.x - 64;
+    const bool rvalid = n0 + ct < N;
+    const uint8_t* srow = W + (size_t)(rvalid ? n0 + ct : 0) * S + K;  // the row's f16 scales
+    // the row's scale exponent from its largest block scale (8 scales per 16-byte load;
+    // the scale area is padded to 16 bytes, lanes past the last block are masked)
+    const int ngroups_row = (nb + 7) / 8;
+    float dmax = 0.0f;
+    if (rvalid) {
+#pragma unroll 4
+      for (int g = 0; g < ngroups_row; ++g) {
+        const int4 v = ld_stream_v4(srow + 16 * g);
+        const uint32_t u[4] = {(uint32_t)v.x, (uint32_t)v.y, (uint32_t)v.z, (uint32_t)v.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (8 * g + i < nb)
+            dmax = fmaxf(dmax, fabsf(__half2float(__ushort_as_half((unsigned short)(u[i >> 1] >> (16 * (i & 1)))))));
+      }
+    }
+    const int eb = split_exponent(dmax);
+    const float up = exp2i(eb);
+    sm.col_scale[ct] = exp2i(-eb);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.scales_ready);
+    // the stages' block scales: 8-block groups (4 stages each) loaded two groups ahead,
+    // counted from this split's first group (sbeg is a multiple of 4 stages)
+    const int ngroups = ngroups_row - gbeg;
+    const uint8_t* sbase = srow + 16 * (size_t)gbeg;
+    const int4 z4 = make_int4(0, 0, 0, 0);
+    int4 g0 = (rvalid && 0 < ngroups) ? ld_stream_v4(sbase) : z4;
+    int4 g1 = (rvalid && 1 < ngroups) ? ld_stream_v4(sbase + 16) : z4;
+    int4 g2 = (rvalid && 2 < ngroups) ? ld_stream_v4(sbase + 32) : z4;
+    for (int s = 0; s < nstages && !*abort; ++s) {
+      const int st = s % kSpStages, bs = s % kSpBSlots;
+      const int gb = 2 * (sbeg + s);  // first block of the stage
+      if ((s & 3) == 0 && s > 0) {
+        const int g = s >> 2;
+        g0 = g1;
+        g1 = g2;
+        g2 = (rvalid && g + 2 < ngroups) ? ld_stream_v4(sbase + 16 * (g + 2)) : z4;
+      }
+      const int q = s & 3;
+      const uint32_t two = (uint32_t)(q == 0 ? g0.x : q == 1 ? g0.y : q == 2 ? g0.z : g0.w);
+      const __half2 s0 = __half2half2(
+          __float2half_rn(__fmul_rn(__half2float(__ushort_as_half((unsigned short)(two & 0xffffu))), up)));
+      const __half2 s1 = __half2half2(__float2half_rn(
+          (gb + 1 < nb) ? __fmul_rn(__half2float(__ushort_as_half((unsigned short)(two >> 16))), up) : 0.0f));
+      if (!mbar_wait(&sm.full[st], (s / kSpStages) & 1, abort)) break;
+      if (s >= kSpBSlots) {
+        const int sp = s - kSpBSlots;
+        if (!mbar_wait(&sm.consumed[sp % kSpStages], (sp / kSpStages) & 1, abort)) break;
+      }
+      const uint32_t* b8row = reinterpret_cast<const uint32_t*>(sm.b8[st] + ct * kBK);
+      uint8_t* dh = sm.b[bs][0] + ct * 128;
+      uint8_t* dl = sm.b[bs][1] + ct * 128;
+      // 8 chunks of 8 values; chunks 0-3 are block gb, 4-7 block gb + 1.  The chunk order
+      // rotates with the row so that lanes read different banks.
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = (i + ct) & 7;
+        const uint2 w = *reinterpret_cast<const uint2*>(b8row + 2 * c);
+        uint4 hi, lo;
+        split8_h(w.x, w.y, c < 4 ? s0 : s1, hi, lo);
+        const int sw = (c ^ (ct & 7)) << 4;
+        *reinterpret_cast<uint4*>(dh + sw) = hi;
+        *reinterpret_cast<uint4*>(dl + sw) = lo;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.bfull[bs]);
+    }
+  } else {
+    // ---------------- epilogue: chunk sums in order, then the exact 2^-(ea + eb) ----------------
+    const int ew = warp - kEpiWarp0;
+    const int quad = warp & 3;
+    const int cg = ew >> 2;
+    const int m = m0 + quad * 32 + lane;
+    const bool mvalid = m < M;
+    pdl_wait();  // row_scale comes from the quantize kernel; y may still be read upstream
+    float acc[kEpiCols];
+#pragma unroll
+    for (int j = 0; j < kEpiCols; ++j) acc[j] = 0.0f;
+    for (int c = 0; c < nchunks && !*abort; ++c) {
+      const int buf = c & 1;
+      if (!mbar_wait(&sm.acc_full[buf], (c >> 1) & 1, abort)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)buf * kBN + cg * kEpiCols;
+#pragma unroll
+      for (int cc = 0; cc < kEpiCols; cc += 32) {
+        float v[32];
+        tmem_ld16_issue(taddr + cc, v);
+        tmem_ld16_issue(taddr + cc + 16, v + 16);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[cc + j] = __fadd_rn(acc[cc + j], v[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.acc_empty[buf]);
+    }
+    const bool ok = !*abort && mbar_wait(&sm.scales_ready, 0, abort);
+    const float rs = mvalid ? row_scale[m] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < kEpiCols; ++j) acc[j] = __fmul_rn(acc[j], __fmul_rn(rs, sm.col_scale[cg * kEpiCols + j]));
+    const int nbase = n0 + cg * kEpiCols;
+    float* const yr = y + (size_t)m * N + nbase;
+    if (splits == 1) {
+      if (mvalid && ok) {
+        if ((N & 3) == 0 && nbase + kEpiCols <= N) {
+#pragma unroll
+          for (int j = 0; j < kEpiCols / 4; ++j)
+            reinterpret_cast<float4*>(yr)[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < kEpiCols; ++j)
+            if (nbase + j < N) yr[j] = acc[j];
+        }
+      }
+    } else if (mvalid && ok) {
+      const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+      float4* mine = reinterpret_cast<float4*>(part + (size_t)(tile * splits + split) * (kBM * kBN) +
+                                               (quad * 32 + lane) * kBN + cg * kEpiCols);
+#pragma unroll
+      for (int j = 0; j < kEpiCols / 4; ++j)
+        mine[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kSpTmemCols) : "memory");
+  }
+}
+
+// Activation rows -> Q8_0 (candle's rules) -> exact hi / lo f16 planes of q * d * 2^ea[m]
+// and rs[m] = 2^-ea[m].  One CTA per row: pass 1 finds the row's largest block scale,
+// pass 2 quantizes again (the row is in L2) and writes the planes.
+constexpr int kSqThreads = 256;
+__global__ void __launch_bounds__(kSqThreads)
+quantize_rows_split_kernel(const float* __restrict__ x, int K, __half* __restrict__ ahi, __half* __restrict__ alo,
+                           float* __restrict__ rs) {
+  __shared__ float red[kSqThreads / 32];
+  pdl_launch_dependents();  // the matmul's CTAs may become resident and start their weight work
+  pdl_wait();
+  const int m = blockIdx.x;
+  const int nb = K >> 5;
+  const float* xr = x + (size_t)m * K;
+  float dmax = 0.0f;
+  for (int b = threadIdx.x; b < nb; b += kSqThreads) {
+    float4 v[8];
+    const float4* src = reinterpret_cast<const float4*>(xr + (size_t)b * kQK);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) v[t] = __ldg(src + t);
+    int q[8];
+    __half dh;
+    quantize_block_regs(v, q, dh);
+    dmax = fmaxf(dmax, fabsf(__half2float(dh)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dmax = fmaxf(dmax, __shfl_xor_sync(0xffffffffu, dmax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = dmax;
+  __syncthreads();
+  dmax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kSqThreads / 32; ++i) dmax = fmaxf(dmax, red[i]);
+  const int ea = split_exponent(dmax);
+  const float up = exp2i(ea);
+  if (threadIdx.x == 0) rs[m] = exp2i(-ea);
+  for (int b = threadIdx.x; b < nb; b += kSqThreads) {
+    float4 v[8];
+    const float4* src = reinterpret_cast<const float4*>(xr + (size_t)b * kQK);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) v[t] = __ldg(src + t);
+    int q[8];
+    __half dh;
+    quantize_block_regs(v, q, dh);
+    const float sc = __fmul_rn(__half2float(dh), up);
+    uint4* dhi = reinterpret_cast<uint4*>(ahi + (size_t)m * K + (size_t)b * kQK);
+    uint4* dlo = reinterpret_cast<uint4*>(alo + (size_t)m * K + (size_t)b * kQK);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      uint4 hi, lo;
+      split8((uint32_t)q[2 * t], (uint32_t)q[2 * t + 1], sc, hi, lo);
+      dhi[t] = hi;
+      dlo[t] = lo;
+    }
+  }
+}
+
 // y[m][n] = sum over splits, in split order, of the partial tiles the split-K matmul
 // wrote: part[tile][split][128][128], tile = (m / 128) * tiles_n + n / 128.  Thread i
 // sums four consecutive columns of one row (tile rows are 128 columns wide, so the
@@ -603,15 +998,103 @@ int tc_splits(int M, int N, int K) {
 
 size_t gemm_tc_smem_bytes() { return sizeof(Smem) + 1024; }
 
-// [qh f16 M x K][dxT f32 nb x Mp][split partials: one wave of 128 x 128 tiles]
+// Which f16 tensor-core kernel serves M > 32: the per-block rescale kernel (default,
+// faster on B200: gate_up 2048 -> 12288 at M = 4096 in 752 us against 1047 us) or the
+// exact-halves kernel (Q8LIN_F16_GEMM=split).  Read once.
+bool f16_split_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("Q8LIN_F16_GEMM");
+    return v && v[0] == 's';
+  }();
+  return on;
+}
+// Stages per TMEM chunk of the exact-halves kernel.  The tensor cores' f32 accumulation
+// over one long K range loses accuracy (measured against the oracle: rel-L2 7e-6 at
+// K = 2048 and 2.1e-5 at K = 6144 in one chunk); chunks of 4 stages (256 K values) added
+// on the CUDA cores keep it near 1e-6 at every K.  Q8LIN_SPLIT_CHUNK overrides (0: one
+// chunk).
+int split_chunk_stages() {
+  static const int c = [] {
+    const char* v = getenv("Q8LIN_SPLIT_CHUNK");
+    return v ? atoi(v) : 4;
+  }();
+  return c;
+}
+
+// per-block kernel: [qh f16 M x K][dxT f32 nb x Mp][split partials: one wave of tiles];
+// exact-halves kernel: [a_hi f16 M x K][a_lo f16 M x K][2^-ea f32 M][split partials]
 size_t gemm_tc_workspace_bytes(int64_t m, int64_t k) {
+  const size_t partials = (size_t)kSplitMaxCtas * kBM * kBN * 4;
+  if (f16_split_enabled()) return 2 * up256((size_t)(m * k) * 2) + up256((size_t)m * 4) + partials;
   const size_t qh = up256((size_t)(m * k) * 2);
   const size_t dx = up256((size_t)(padded_rows(m) * (k / kQK)) * 4);
-  return qh + dx + (size_t)kSplitMaxCtas * kBM * kBN * 4;
+  return qh + dx + partials;
+}
+
+static cudaError_t launch_gemm_split(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
+                                     cudaStream_t s) {
+  const int M = (int)m, K = (int)w.k, N = (int)w.n;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const size_t plane = up256((size_t)M * K * 2);
+  __half* ahi = reinterpret_cast<__half*>(ws);
+  __half* alo = reinterpret_cast<__half*>(ws + plane);
+  float* rs = reinterpret_cast<float*>(ws + 2 * plane);
+  float* part = reinterpret_cast<float*>(ws + 2 * plane + up256((size_t)M * 4));
+  const int splits = tc_splits(M, N, K);
+
+  CUtensorMap map_ahi, map_alo, map_b;
+  if (!encode_2d(&map_ahi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, ahi, K, M, (uint64_t)K * 2, kBK, kBM,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&map_alo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, alo, K, M, (uint64_t)K * 2, kBK, kBM,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.packed, K, N, (uint64_t)w.row_stride, kBK, kBN,
+                 CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)M);
+    cfg.blockDim = dim3(kSqThreads);
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, quantize_rows_split_kernel, x, K, ahi, alo, rs);
+    if (e != cudaSuccess) return e;
+  }
+  const size_t smem = sizeof(SpSmem) + 1024;
+  static int configured[128] = {0};
+  {
+    cudaError_t e = ensure_smem((const void*)gemm_q8_0_split_kernel, configured, w.device, smem, false);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM), (unsigned)splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_q8_0_split_kernel, map_ahi, map_alo, map_b,
+                                     (const uint8_t*)w.packed, w.row_stride, N, K, (const float*)rs, y, M, splits,
+                                     part, split_chunk_stages(), wait_limit_ns());
+  if (e != cudaSuccess || splits == 1) return e;
+  const int tiles_n = (N + kBN - 1) / kBN;
+  const int64_t work = (int64_t)M * tiles_n * (kBN / 4);
+  cudaLaunchConfig_t rcfg = {};
+  rcfg.gridDim = dim3((unsigned)((work + 255) / 256));
+  rcfg.blockDim = dim3(256);
+  rcfg.stream = s;
+  rcfg.attrs = attr;
+  rcfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&rcfg, tc_split_reduce_kernel, (const float*)part, splits, M, N, tiles_n, y);
 }
 
 cudaError_t launch_gemm_tc(const q8lin_weight& w, const float* x, void* workspace, float* y, int64_t m,
                            cudaStream_t s) {
+  if (f16_split_enabled()) return launch_gemm_split(w, x, workspace, y, m, s);
   const int M = (int)m, K = (int)w.k, N = (int)w.n;
   const int Mp = (int)padded_rows(m);
   const int nb = K / kQK;

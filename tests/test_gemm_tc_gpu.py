@@ -80,3 +80,33 @@ def test_tc_fault_word_clear(cuda_device):
     flags = ctypes.c_uint32(123)
     _lib.check(_lib.lib().q8lin_fault_status(0, ctypes.byref(flags), 1))
     assert flags.value == 0
+
+
+def test_split_kernel_matches_oracle(cuda_device):
+    """The exact-halves kernel (Q8LIN_F16_GEMM=split, read once per process, so in a child):
+    parity with the oracle on a partial tile, an odd block count (last stage with one
+    block), split-K and a long K over several 4-stage TMEM chunks."""
+    import os
+    import subprocess
+    import sys
+    import textwrap
+
+    code = textwrap.dedent("""
+        import numpy as np, torch
+        from talechime_b200 import QMatMul, _lib, synth
+        import oracle
+        from tests.conftest import assert_close_to_oracle
+        dev = torch.device("cuda", 0)
+        for m, k, n in ((64, 2048, 2048), (100, 2080, 300), (33, 4096, 512), (200, 6144, 640)):
+            assert _lib.PATH_NAMES[_lib.lib().q8lin_dispatch_path(m, k, n)] == "f16_tc"
+            w = synth.q8_0_blocks(np.random.default_rng(m + k + n), n, k)
+            q = QMatMul.from_gguf_blocks(w, n, k, device=dev)
+            x = np.random.default_rng(m).standard_normal((m, k), dtype=np.float32)
+            y = q.forward(torch.from_numpy(x).to(dev)).cpu().numpy()
+            assert_close_to_oracle(y, oracle.matmul(x, w, n, threads=16))
+        print("ok")
+    """)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, Q8LIN_F16_GEMM="split", PYTHONPATH=root)
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
