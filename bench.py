@@ -572,6 +572,36 @@ def run_decoder_prefill(torch, dist, dev, rank: int, world: int, batch: int = 4,
             "linear_gflop": linear_flops / 1e9, "attention_gflop": attn_flops / 1e9}
 
 
+def run_profile_prefill(args) -> None:
+    """A short prompt pass for ncu captures: `--profile-prefill B:T` prefills B sequences
+    of T random ids through a decoder of `--layers` layers (max_t = T), once as warm-up
+    (launches to skip with ncu -s) and once timed."""
+    import torch
+    from talechime_b200 import build
+    from talechime_b200.decoder import DecoderConfig, Q8Decoder, synthetic_weights
+
+    build.build()
+    b, t = (int(v) for v in args.profile_prefill.split(":"))
+    dev = torch.device("cuda", 0)
+    cfg = DecoderConfig(layers=args.layers, max_t=t)
+    weights = synthetic_weights(cfg, seed=4242, device=dev)
+    dec = Q8Decoder(cfg, weights, device=dev, batch=b)
+    del weights
+    ids = torch.randint(0, cfg.vocab, (b, t), generator=torch.Generator().manual_seed(5))
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        dec.prefill(ids)
+        torch.cuda.synchronize(dev)
+        dec.reset()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dec.prefill(ids)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    print(json.dumps({"profile_prefill": {"batch": b, "tokens": t}, "layers": cfg.layers,
+                      "ms": e0.elapsed_time(e1), "note": "profiling run; not a bench line"}), flush=True)
+
+
 def run_profile_decoder(args) -> None:
     """A short decoder run for ncu captures: 4 eager steps (warm-up launches to skip with
     ncu -s), then 8 steps replayed from one CUDA graph, from position 380."""
@@ -627,6 +657,8 @@ def main() -> None:
                     help="M:K:N -- run one projection shape `--steps` times (profiling), print its timing")
     ap.add_argument("--sweep", action="store_true",
                     help="also time the BASELINE configs[1] shape sweep (M x {qkv,o,gate_up,down}) into the line")
+    ap.add_argument("--profile-prefill", default=None, metavar="B:T",
+                    help="ncu helper: one warm-up and one timed prompt pass of B x T tokens (--layers layers)")
     ap.add_argument("--profile-decoder", default=None, choices=["fused", "persistent", "unfused"],
                     help="profiling run: only the decoder, `--layers` layers, 8 steps replayed from a graph "
                          "after 4 eager warm-up steps from position 380; prints its timing")
@@ -649,6 +681,9 @@ def main() -> None:
         return
     if args.profile_decoder:
         run_profile_decoder(args)
+        return
+    if args.profile_prefill:
+        run_profile_prefill(args)
         return
 
     torch.cuda.set_device(local_rank)

@@ -155,10 +155,11 @@ add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ y, const flo
 //   * q rows staged once, K / V tiles double-buffered in shared memory (cp.async, rows
 //     past the sequence's pos0 + T valid rows zero-filled, so no stale cache row can
 //     reach the sums);
-//   * thread (ty, tx) of 16 x 16 holds the scores of rows ty + 16a and keys tx + 16b
+//   * thread (ty, tx) of 16 x 16 holds the scores of rows 4ty + a and keys tx + 16b
 //     (a, b < 4; q / k rows padded to 132 floats: every 8-lane phase of a 16-byte
-//     shared load hits 32 distinct banks) and the output of rows ty + 16a, dimensions
-//     tx*4 .. +4 and 64 + tx*4 .. +4;
+//     shared load hits 32 distinct banks) and the output of rows 4ty + a, dimensions
+//     tx*4 .. +4 and 64 + tx*4 .. +4; probabilities are stored key-major, so one
+//     16-byte load gives a key's four rows;
 //   * per tile: scores, the causal mask, a running max / sum per row (online softmax,
 //     the 16 lanes of a row reduced with xor shuffles), probabilities through shared
 //     memory, O += P V;
@@ -168,13 +169,13 @@ constexpr int kPfKeys = 64;
 constexpr int kPfThreads = 256;
 constexpr int kPfD = 128;
 constexpr int kPfQStride = 132;
-constexpr int kPfPStride = 80;  // (16 * ty) mod 32 separates the two rows of a warp
+constexpr int kPfPStride = 68;  // key-major probabilities: 64 rows + 4 floats of padding
 
 struct PfSmem {
   alignas(16) float q[kPfRows][kPfQStride];
   alignas(16) float k[2][kPfKeys][kPfQStride];
   alignas(16) float v[2][kPfKeys][kPfD];
-  alignas(16) float p[kPfRows][kPfPStride];
+  alignas(16) float p[kPfKeys][kPfPStride];
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -245,7 +246,7 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
     }
     __syncthreads();
 
-    // scores of rows ty + 16a against keys tx + 16b
+    // scores of rows 4ty + a against keys tx + 16b
     float s[4][4];
 #pragma unroll
     for (int a = 0; a < 4; ++a)
@@ -255,7 +256,7 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
     for (int d4 = 0; d4 < kPfD / 4; ++d4) {
       float4 qa[4], kb[4];
 #pragma unroll
-      for (int a = 0; a < 4; ++a) qa[a] = *reinterpret_cast<const float4*>(&sm.q[ty + 16 * a][d4 * 4]);
+      for (int a = 0; a < 4; ++a) qa[a] = *reinterpret_cast<const float4*>(&sm.q[4 * ty + a][d4 * 4]);
 #pragma unroll
       for (int bb = 0; bb < 4; ++bb) kb[bb] = *reinterpret_cast<const float4*>(&sm.k[buf][tx + 16 * bb][d4 * 4]);
 #pragma unroll
@@ -275,7 +276,7 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
     const int j0 = kt * kPfKeys;
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
-      const int qpos = pos0 + q0 + ty + 16 * a;  // absolute position of the row
+      const int qpos = pos0 + q0 + 4 * ty + a;  // absolute position of the row
       float mx = -INFINITY;
 #pragma unroll
       for (int bb = 0; bb < 4; ++bb) {
@@ -300,9 +301,10 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[a][e] = __fmul_rn(o[a][e], corr);
       m_run[a] = mn;
-#pragma unroll
-      for (int bb = 0; bb < 4; ++bb) sm.p[ty + 16 * a][tx + 16 * bb] = s[a][bb];
     }
+#pragma unroll
+    for (int bb = 0; bb < 4; ++bb)
+      *reinterpret_cast<float4*>(&sm.p[tx + 16 * bb][4 * ty]) = make_float4(s[0][bb], s[1][bb], s[2][bb], s[3][bb]);
     __syncthreads();
 
     // O += P V over the keys of the tile that some row can see
@@ -311,9 +313,11 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
     for (int j = 0; j < jn; ++j) {
       const float4 v0 = *reinterpret_cast<const float4*>(&sm.v[buf][j][tx * 4]);
       const float4 v1 = *reinterpret_cast<const float4*>(&sm.v[buf][j][64 + tx * 4]);
+      const float4 p4 = *reinterpret_cast<const float4*>(&sm.p[j][4 * ty]);
+      const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
       for (int a = 0; a < 4; ++a) {
-        const float pa = sm.p[ty + 16 * a][j];
+        const float pa = pj[a];
         o[a][0] = __fmaf_rn(pa, v0.x, o[a][0]);
         o[a][1] = __fmaf_rn(pa, v0.y, o[a][1]);
         o[a][2] = __fmaf_rn(pa, v0.z, o[a][2]);
@@ -332,7 +336,7 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
     float l = l_run[a];
 #pragma unroll
     for (int off = 8; off > 0; off >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, off));
-    const int r = ty + 16 * a;
+    const int r = 4 * ty + a;
     if (r < qrows) {
       float* dst = out + (((size_t)b * T + q0 + r) * Hq + h) * kPfD;
       *reinterpret_cast<float4*>(dst + tx * 4) =

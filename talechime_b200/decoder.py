@@ -1,4 +1,5 @@
-"""Batch-1 Q8_0 decoder (the VoxCPM BaseLM-style Llama decoder).
+"""Q8_0 decoder (BASELINE configs[2] and [3]: the VoxCPM BaseLM-style Llama decoder):
+batch-1 decode steps and a batched prompt pass (``prefill``).
 
 Per layer (crates/voxcpm/src/transformer.rs:107-155): rms_norm -> fused q|k|v Q8_0 linear
 -> RoPE on q and k, k and v appended to the f32 KV cache -> attention over the cache ->
