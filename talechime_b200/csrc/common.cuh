@@ -241,7 +241,8 @@ __device__ __forceinline__ float block_term(const uint8_t* row, int K, int blk, 
   const int h = half_order(threadIdx.x & 31) * 16;
   const int4 w0 = *reinterpret_cast<const int4*>(row + (size_t)blk * 32 + h);
   const int4 w1 = *reinterpret_cast<const int4*>(row + (size_t)blk * 32 + (16 - h));
-  const int isum = dot16(w1, x1, dot16(w0, x0, 0));  // exact in int32 either way
+  // two independent 4-deep dp4a chains (exact in int32 in any order)
+  const int isum = dot16(w0, x0, 0) + dot16(w1, x1, 0);
   const float dw = __half2float(reinterpret_cast<const __half*>(row + K)[blk]);
   return __fmul_rn(__fmul_rn(__int2float_rn(isum), dw), dxs);
 }
@@ -327,7 +328,8 @@ __device__ __forceinline__ float block_term_s(uint32_t row, int K, int blk, cons
   const uint32_t b = row + (uint32_t)blk * 32u;
   const int4 w0 = lds128(b + h);
   const int4 w1 = lds128(b + (16u - h));
-  const int isum = dot16(w1, x1, dot16(w0, x0, 0));  // exact in int32 either way
+  // two independent 4-deep dp4a chains (exact in int32 in any order)
+  const int isum = dot16(w0, x0, 0) + dot16(w1, x1, 0);
   const float dw = lds_half_f32(row + (uint32_t)K + 2u * (uint32_t)blk);
   return __fmul_rn(__fmul_rn(__int2float_rn(isum), dw), dxs);
 }

@@ -462,15 +462,32 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n, float* __
     last = (atomicAdd(cnt, 1u) == gridDim.x - 1) ? 1 : 0;
   }
   __syncthreads();
-  if (last && threadIdx.x == 0) {
+  if (last) {
+    // the last CTA reduces the per-CTA partials with all of its threads (same order
+    // rule: larger value, then lower index)
     __threadfence();
-    float v = pv[0];
-    int ix = pi[0];
-    for (int b = 1; b < (int)gridDim.x; ++b)
-      if (pv[b] > v || (pv[b] == v && pi[b] < ix)) { v = pv[b]; ix = pi[b]; }
-    *token = ix < n ? ix : 0;
-    if (pos_dev) *pos_dev += 1;
-    *cnt = 0;
+    float v = -INFINITY;
+    int ix = n;
+    for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) {
+      const float pvb = __ldcg(pv + b);
+      const int pib = __ldcg(pi + b);
+      if (pvb > v || (pvb == v && pib < ix)) { v = pvb; ix = pib; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(kFull, v, o);
+      const int oi = __shfl_xor_sync(kFull, ix, o);
+      if (ov > v || (ov == v && oi < ix)) { v = ov; ix = oi; }
+    }
+    __syncthreads();  // every thread has read sv / si of the first phase
+    if (lane == 0) { sv[warp] = v; si[warp] = ix; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+        if (sv[w] > v || (sv[w] == v && si[w] < ix)) { v = sv[w]; ix = si[w]; }
+      *token = ix < n ? ix : 0;
+      if (pos_dev) *pos_dev += 1;
+      *cnt = 0;
+    }
   }
 }
 
