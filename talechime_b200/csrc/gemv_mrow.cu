@@ -10,8 +10,8 @@
 //     wait -- as the M = 1 kernel, and for the same reasons: a thread's TMA / bulk copies
 //     complete one after another on B200, and a warp that consumes its own slots in
 //     order needs no mbarrier parity;
-//   * the CTA quantizes the M activation rows into shared memory (candle's rules, one
-//     thread per block), then each warp takes two weight rows at a time against every
+//   * the CTA quantizes the M activation rows into shared memory (candle's rules, 8
+//     lanes per block), then each warp takes two weight rows at a time against every
 //     activation row: lane l owns blocks l and l + 32 of each 2048-value segment, loads the
 //     two rows' blocks once (per-lane half order: conflict-free) and, per activation row
 //     m, the activation blocks, accumulating ((f32(isum) * dw) * dx) per block (each
@@ -102,22 +102,32 @@ gemv_q8_0_mrow_kernel(const uint8_t* __restrict__ W, int64_t S, int N, int K, in
 
   pdl_wait();
   {
-    // quantize the M activation rows, one thread per 32-value block (rows >= M stay
-    // unread: the row loop skips them)
-    const int blocks = M * nb;
-    for (int i = threadIdx.x; i < blocks; i += kMrThreads) {
-      const int m = i / nb, b = i - m * nb;
-      const float4* src = reinterpret_cast<const float4*>(x + (size_t)m * K + (size_t)b * kQK);
-      float4 v[8];
+    // quantize the M activation rows (rows >= M stay unread: the row loop skips them):
+    // 8 lanes per 32-value block, 4 values each (x is [M][K] row-major, so quad i of the
+    // flattened rows is values 4i .. 4i + 3 and 8 consecutive quads form one block); the
+    // loads of up to four passes of the CTA are issued before any is quantized
+    constexpr int kPass = 4;
+    const int nquads = M * (K >> 2);
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (int base = 0; base < nquads; base += kPass * kMrThreads) {  // uniform over the CTA
+      float4 v[kPass];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) v[t] = __ldg(src + t);
-      int q[8];
-      __half dh;
-      quantize_block_regs(v, q, dh);
-      int4* dst = reinterpret_cast<int4*>(qx + (size_t)m * K + (size_t)b * kQK);
-      dst[0] = make_int4(q[0], q[1], q[2], q[3]);
-      dst[1] = make_int4(q[4], q[5], q[6], q[7]);
-      dx[m * nb + b] = __half2float(dh);
+      for (int g = 0; g < kPass; ++g) {
+        const int i = base + g * kMrThreads + threadIdx.x;
+        v[g] = i < nquads ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int g = 0; g < kPass; ++g) {
+        if (base + g * kMrThreads < nquads) {  // uniform: every lane takes part in the shuffles
+          const int i = base + g * kMrThreads + threadIdx.x;
+          __half dh;
+          const int q = quantize_octet(v[g], dh);
+          if (i < nquads) {
+            reinterpret_cast<int*>(qx)[i] = q;  // qx rows are K apart: quad i lands at 4i
+            if ((i & 7) == 0) dx[i >> 3] = __half2float(dh);  // block i / 8 = m * nb + b
+          }
+        }
+      }
     }
   }
   __syncthreads();
