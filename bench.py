@@ -441,8 +441,9 @@ def run_tp_mlp(torch, dist, dev, rank: int, world: int, reps: int = 20) -> dict:
 def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, steps: int = 512) -> dict:
     """Config 2: the ~2B Q8_0 decoder (hidden 2048, 28 layers, 16 x 128 heads, SwiGLU 6144,
     RMSNorm, RoPE, f32 KV cache, vocab 73448; talechime_b200/decoder.py), batch 1: a
-    128-token random-id prefix run as one batched forward (Q8Decoder.prefill, timed on its
-    own), then `steps` greedy decode steps replayed from one CUDA graph of a step; device
+    128-token random-id prefix run as one batched forward (Q8Decoder.prefill: device time
+    from a CUDA graph of its launches, and the median wall time of 5 host-issued calls),
+    then `steps` greedy decode steps replayed from one CUDA graph of a step; device
     time of the decode steps (CUDA events), max over ranks (one independent replica per
     GPU).  Both step implementations are timed: "fused" (one launch per operation, the
     default) and "persistent" (one cooperative launch per step)."""
@@ -465,13 +466,31 @@ def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, step
         dec.reset(ids[0])
         dec.prefill(ids)  # warm-up: workspace growth and kernel attributes
         torch.cuda.synchronize(dev)
+        # as the user calls it (host-issued launches, one position read-back): median of 5
+        host_ms = []
+        for _ in range(5):
+            dec.reset(ids[0])
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            dec.prefill(ids)
+            torch.cuda.synchronize(dev)
+            host_ms.append((time.perf_counter() - t0) * 1e3)
+        # device time: the same launches captured once in a CUDA graph and replayed
+        tok_d = torch.tensor(ids, dtype=torch.int32, device=dev)
+        pgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(pgraph, stream=stream):
+            dec._prefill_launches(tok_d, 1, prefix, 0)
+        pgraph.replay()
+        torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        dec.reset(ids[0])
         e0.record(stream)
-        dec.prefill(ids)
+        for _ in range(5):
+            pgraph.replay()
         e1.record(stream)
         torch.cuda.synchronize(dev)
-    prefill_ms = e0.elapsed_time(e1)
+        del pgraph
+    prefill_ms = e0.elapsed_time(e1) / 5
+    prefill_host_ms = statistics.median(host_ms)
     for mode in ("fused", "persistent"):
         with torch.cuda.stream(stream):
             dec.reset(ids[0])
@@ -505,6 +524,7 @@ def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, step
                      f"f32 KV cache, vocab 73448; batch 1, {prefix}-token random-id prefix (one batched forward), "
                      f"{steps} greedy steps",
            "prefix_prefill_ms": prefill_ms, "prefix_prefill_tokens_per_s": prefix / (prefill_ms * 1e-3),
+           "prefix_prefill_host_issued_ms": prefill_host_ms,
            "tokens_per_s": world * steps / (ms * 1e-3), "ms_per_token": ms / steps,
            "tokens_per_s_persistent": world * steps / (msp * 1e-3), "ms_per_token_persistent": msp / steps,
            "weight_bytes_per_token": wbytes, "kv_bytes_per_token_avg": kv_bytes / steps,

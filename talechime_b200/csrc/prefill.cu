@@ -150,41 +150,46 @@ add_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ y, const flo
 }
 
 // ---------------------------------------------------------------------------------
-// attention_prefill: grid (ceil(T / 64), Hq, B), 256 threads; one CTA = 64 query rows
+// attention_prefill: grid (ceil(T / 16A), Hq, B), 256 threads; one CTA = 16A query rows
 // of one head of one sequence, flash-style over 64-key tiles of the cache:
 //   * q rows staged once, K / V tiles double-buffered in shared memory (cp.async, rows
 //     past the sequence's pos0 + T valid rows zero-filled, so no stale cache row can
 //     reach the sums);
-//   * thread (ty, tx) of 16 x 16 holds the scores of rows 4ty + a and keys tx + 16b
-//     (a, b < 4; q / k rows padded to 132 floats: every 8-lane phase of a 16-byte
-//     shared load hits 32 distinct banks) and the output of rows 4ty + a, dimensions
+//   * thread (ty, tx) of 16 x 16 holds the scores of rows A*ty + a and keys tx + 16b
+//     (a < A, b < 4; q / k rows padded to 132 floats: every 8-lane phase of a 16-byte
+//     shared load hits 32 distinct banks) and the output of rows A*ty + a, dimensions
 //     tx*4 .. +4 and 64 + tx*4 .. +4; probabilities are stored key-major, so one
-//     16-byte load gives a key's four rows;
+//     load gives a key's A rows;
 //   * per tile: scores, the causal mask, a running max / sum per row (online softmax,
 //     the 16 lanes of a row reduced with xor shuffles), probabilities through shared
 //     memory, O += P V;
 //   * out = O / sum.  Query tiles are taken longest first (blockIdx.x reversed).
-constexpr int kPfRows = 64;
+// A rows per thread: 64-row query tiles (A = 4), or 32-row tiles (A = 2) where the
+// 64-row grid would occupy fewer than half of the SMs (a short prompt, one sequence).
 constexpr int kPfKeys = 64;
 constexpr int kPfThreads = 256;
 constexpr int kPfD = 128;
 constexpr int kPfQStride = 132;
-constexpr int kPfPStride = 68;  // key-major probabilities: 64 rows + 4 floats of padding
 
+template <int A>
 struct PfSmem {
-  alignas(16) float q[kPfRows][kPfQStride];
+  static constexpr int kRows = 16 * A;
+  static constexpr int kPStride = kRows + 4;  // key-major probabilities, padded
+  alignas(16) float q[kRows][kPfQStride];
   alignas(16) float k[2][kPfKeys][kPfQStride];
   alignas(16) float v[2][kPfKeys][kPfD];
-  alignas(16) float p[kPfKeys][kPfPStride];
+  alignas(16) float p[kPfKeys][kPStride];
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+template <int A>
 __global__ void __launch_bounds__(kPfThreads, 1)
 attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                          int T, int pos0, int Hq, int Hkv, int max_t, float scale, float* __restrict__ out) {
+  constexpr int kPfRows = PfSmem<A>::kRows;
   extern __shared__ __align__(16) uint8_t pf_smem[];
-  PfSmem& sm = *reinterpret_cast<PfSmem*>(pf_smem);
+  PfSmem<A>& sm = *reinterpret_cast<PfSmem<A>*>(pf_smem);
   pdl_launch_dependents();  // dependents may become resident now; they wait for this grid
   const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
@@ -226,10 +231,10 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
   };
   load_kv(0, 0);  // the q copies travel in the first group
 
-  float o[4][8];
-  float m_run[4], l_run[4];
+  float o[A][8];
+  float m_run[A], l_run[A];
 #pragma unroll
-  for (int a = 0; a < 4; ++a) {
+  for (int a = 0; a < A; ++a) {
     m_run[a] = -INFINITY;
     l_run[a] = 0.0f;
 #pragma unroll
@@ -246,21 +251,21 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
     }
     __syncthreads();
 
-    // scores of rows 4ty + a against keys tx + 16b
-    float s[4][4];
+    // scores of rows A*ty + a against keys tx + 16b
+    float s[A][4];
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < A; ++a)
 #pragma unroll
       for (int bb = 0; bb < 4; ++bb) s[a][bb] = 0.0f;
 #pragma unroll 4
     for (int d4 = 0; d4 < kPfD / 4; ++d4) {
-      float4 qa[4], kb[4];
+      float4 qa[A], kb[4];
 #pragma unroll
-      for (int a = 0; a < 4; ++a) qa[a] = *reinterpret_cast<const float4*>(&sm.q[4 * ty + a][d4 * 4]);
+      for (int a = 0; a < A; ++a) qa[a] = *reinterpret_cast<const float4*>(&sm.q[A * ty + a][d4 * 4]);
 #pragma unroll
       for (int bb = 0; bb < 4; ++bb) kb[bb] = *reinterpret_cast<const float4*>(&sm.k[buf][tx + 16 * bb][d4 * 4]);
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
+      for (int a = 0; a < A; ++a)
 #pragma unroll
         for (int bb = 0; bb < 4; ++bb) {
           float acc = s[a][bb];
@@ -275,8 +280,8 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
     // causal mask, online softmax; probabilities to shared memory
     const int j0 = kt * kPfKeys;
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
-      const int qpos = pos0 + q0 + 4 * ty + a;  // absolute position of the row
+    for (int a = 0; a < A; ++a) {
+      const int qpos = pos0 + q0 + A * ty + a;  // absolute position of the row
       float mx = -INFINITY;
 #pragma unroll
       for (int bb = 0; bb < 4; ++bb) {
@@ -303,8 +308,12 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
       m_run[a] = mn;
     }
 #pragma unroll
-    for (int bb = 0; bb < 4; ++bb)
-      *reinterpret_cast<float4*>(&sm.p[tx + 16 * bb][4 * ty]) = make_float4(s[0][bb], s[1][bb], s[2][bb], s[3][bb]);
+    for (int bb = 0; bb < 4; ++bb) {
+      if constexpr (A == 4)
+        *reinterpret_cast<float4*>(&sm.p[tx + 16 * bb][4 * ty]) = make_float4(s[0][bb], s[1][bb], s[2][bb], s[3][bb]);
+      else
+        *reinterpret_cast<float2*>(&sm.p[tx + 16 * bb][2 * ty]) = make_float2(s[0][bb], s[1][bb]);
+    }
     __syncthreads();
 
     // O += P V over the keys of the tile that some row can see
@@ -313,10 +322,16 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
     for (int j = 0; j < jn; ++j) {
       const float4 v0 = *reinterpret_cast<const float4*>(&sm.v[buf][j][tx * 4]);
       const float4 v1 = *reinterpret_cast<const float4*>(&sm.v[buf][j][64 + tx * 4]);
-      const float4 p4 = *reinterpret_cast<const float4*>(&sm.p[j][4 * ty]);
-      const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
+      float pj[A];
+      if constexpr (A == 4) {
+        const float4 p4 = *reinterpret_cast<const float4*>(&sm.p[j][4 * ty]);
+        pj[0] = p4.x, pj[1] = p4.y, pj[2] = p4.z, pj[3] = p4.w;
+      } else {
+        const float2 p2 = *reinterpret_cast<const float2*>(&sm.p[j][2 * ty]);
+        pj[0] = p2.x, pj[1] = p2.y;
+      }
 #pragma unroll
-      for (int a = 0; a < 4; ++a) {
+      for (int a = 0; a < A; ++a) {
         const float pa = pj[a];
         o[a][0] = __fmaf_rn(pa, v0.x, o[a][0]);
         o[a][1] = __fmaf_rn(pa, v0.y, o[a][1]);
@@ -332,11 +347,11 @@ attention_prefill_kernel(const float* __restrict__ q, const float* __restrict__ 
   }
 
 #pragma unroll
-  for (int a = 0; a < 4; ++a) {
+  for (int a = 0; a < A; ++a) {
     float l = l_run[a];
 #pragma unroll
     for (int off = 8; off > 0; off >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, off));
-    const int r = 4 * ty + a;
+    const int r = A * ty + a;
     if (r < qrows) {
       float* dst = out + (((size_t)b * T + q0 + r) * Hq + h) * kPfD;
       *reinterpret_cast<float4*>(dst + tx * 4) =
@@ -387,17 +402,31 @@ cudaError_t launch_add_rmsnorm(float* x, const float* y, const float* w, float e
   return e != cudaSuccess ? e : launch_rmsnorm(x, w, eps, m, n, h, s);
 }
 
-cudaError_t launch_attention_prefill(const float* q, const float* kc, const float* vc, int batch, int t, int pos0,
-                                     int hq, int hkv, int max_t, float* out, int device, cudaStream_t s) {
+template <int A>
+static cudaError_t launch_attention_prefill_a(const float* q, const float* kc, const float* vc, int batch, int t,
+                                             int pos0, int hq, int hkv, int max_t, float* out, int device,
+                                             cudaStream_t s) {
   static int configured[128] = {0};
-  cudaError_t e = ensure_smem((const void*)attention_prefill_kernel, configured, device, sizeof(PfSmem), false);
+  cudaError_t e =
+      ensure_smem((const void*)attention_prefill_kernel<A>, configured, device, sizeof(PfSmem<A>), false);
   if (e != cudaSuccess) return e;
+  constexpr int rows = PfSmem<A>::kRows;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = pf_cfg(dim3((unsigned)((t + kPfRows - 1) / kPfRows), (unsigned)hq, (unsigned)batch),
-                                  dim3(kPfThreads), sizeof(PfSmem), s, attr);
+  cudaLaunchConfig_t cfg = pf_cfg(dim3((unsigned)((t + rows - 1) / rows), (unsigned)hq, (unsigned)batch),
+                                  dim3(kPfThreads), sizeof(PfSmem<A>), s, attr);
   // candle's `scores / sqrt(width)` multiplies by the f32 rounding of 1/sqrt(width)
   const float scale = (float)(1.0 / std::sqrt(128.0));
-  return cudaLaunchKernelEx(&cfg, attention_prefill_kernel, q, kc, vc, t, pos0, hq, hkv, max_t, scale, out);
+  return cudaLaunchKernelEx(&cfg, attention_prefill_kernel<A>, q, kc, vc, t, pos0, hq, hkv, max_t, scale, out);
+}
+
+cudaError_t launch_attention_prefill(const float* q, const float* kc, const float* vc, int batch, int t, int pos0,
+                                     int hq, int hkv, int max_t, float* out, int device, cudaStream_t s) {
+  // measured on B200 (one sequence, 16 heads, us): 32-row tiles take T = 128 from 20.7 to
+  // 15.7, but T = 512 from 70.4 to 84.5 and T = 1024 (GQA 16:2) from 210 to 242
+  const int64_t ctas64 = (int64_t)((t + 63) / 64) * hq * batch;
+  if (2 * ctas64 < (int64_t)sm_count(device))
+    return launch_attention_prefill_a<2>(q, kc, vc, batch, t, pos0, hq, hkv, max_t, out, device, s);
+  return launch_attention_prefill_a<4>(q, kc, vc, batch, t, pos0, hq, hkv, max_t, out, device, s);
 }
 
 }  // namespace q8lin

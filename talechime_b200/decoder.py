@@ -335,11 +335,17 @@ class Q8Decoder:
             raise _lib.Q8LinError(_lib.ERR_SHAPE, "prefill needs at least one token")
         if pos0 + T > cfg.max_t:
             raise _lib.Q8LinError(_lib.ERR_SHAPE, "Transformer context limit exceeded")
+        return self._prefill_launches(tok.reshape(-1).to(self.device), B, T, pos0)
+
+    def _prefill_launches(self, tok_d: torch.Tensor, B: int, T: int, pos0: int) -> torch.Tensor:
+        """The device work of ``prefill`` for `tok_d` (int32 [B * T] on the device) at a
+        host-known position pos0 (checked by the caller): kernel launches on the current
+        stream and tensor allocations only, no host synchronisation."""
+        cfg, L, P = self.cfg, _lib.lib(), self._p
         dev, H, M = self.device, cfg.hidden, B * T
         hd = cfg.heads * cfg.head_dim
         s = ctypes.c_void_p(_stream_ptr(dev))
         e = lambda *shape: torch.empty(shape, dtype=torch.float32, device=dev)
-        tok_d = tok.reshape(-1).to(dev)
         x, hn, qkv, q, att, t1 = e(M, H), e(M, H), e(M, cfg.qkv_rows), e(M, hd), e(M, hd), e(M, H)
         gu, hm = e(M, 2 * cfg.inter), e(M, cfg.inter)
         check(L.q8lin_embed_rows(self.embed.handle, P(tok_d), M, P(x), s))

@@ -115,6 +115,7 @@ def _attention_np(q, kc, vc, T, pos0, hq, hkv):
     (1, 130, 5, 16, 2, 160),   # three query tiles, the last with 2 rows
     (3, 65, 0, 8, 8, 80),      # no grouping, a 1-row last tile
     (1, 200, 300, 2, 1, 512),  # long history before the new rows
+    (6, 200, 10, 16, 16, 256),  # 384 CTAs at 64-row tiles (the cases above take 32-row tiles)
 ])
 def test_attention_prefill_matches_masked_softmax(cuda_device, B, T, pos0, hq, hkv, max_t):
     """Cache rows past pos0 + T hold NaN: the kernel must never let them into a sum."""
