@@ -201,8 +201,9 @@ attention_decode_kernel(const float* __restrict__ q, const float* __restrict__ k
 //   * streams its cached K and V rows through a two-slot shared-memory ring of
 //     kRaChunk-row chunks (cp.async.bulk from this GPU's memory, mbarrier complete_tx),
 //     the copy of chunk c + 2 issued as soon as chunk c is consumed;
-//   * per chunk: scores (one warp per 4 positions), a running max / sum / weighted V
-//     sum (online softmax; 256 threads = 128 dims x 2 position halves);
+//   * per chunk: each warp takes 4 positions and keeps its own online softmax (running
+//     max and sum, and the weighted V sum of each lane's 4 dimensions); one barrier per
+//     chunk frees the slot; after the last chunk the 8 warps are merged in warp order;
 //   * publishes its (max, sum, acc[128]) in shared memory; after a cluster barrier CTA
 //     rank 0 reads the partials of the cluster through distributed shared memory, merges
 //     them in rank order and writes the output; a second barrier keeps every CTA's
@@ -219,10 +220,10 @@ struct RaSmem {
   alignas(16) float q[128];
   alignas(16) float kcur[128];
   alignas(16) float vcur[128];
-  alignas(16) float acc2[2][128];
   alignas(16) float pacc[128];  // this CTA's partial: weighted V sum
-  float sc[kRaChunk];
-  float stat[4];  // running max, running sum, chunk correction, partial max
+  alignas(16) float wacc[kRaThreads / 32][128];  // each warp's weighted V sum
+  float wm[kRaThreads / 32], wl[kRaThreads / 32];  // each warp's running max and sum
+  float stat[4];  // [3]: this CTA's partial max
   float pl;       // partial sum
   alignas(8) uint64_t full[2];
 };
@@ -320,19 +321,17 @@ rope_attention_kernel(const float* __restrict__ qkv, const int* __restrict__ pos
       }
     }
   }
-  if (tid == 0) {
-    sm.stat[0] = -INFINITY;
-    sm.stat[1] = 0.0f;
-  }
   __syncthreads();
+  // Warp w owns positions 4w .. 4w+3 of every chunk and keeps its own online softmax: a
+  // running max m and sum l (the same in every lane) and the weighted V sum of the
+  // lane's four dimensions; the warps are merged once, after the last chunk.
   const float4 q4 = reinterpret_cast<const float4*>(sm.q)[lane];
-  const int d = tid & 127, hh = tid >> 7;
-  float acc = 0.0f;  // weighted V sum of dimension d over this thread's position half
+  float m = -INFINITY, l = 0.0f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   bool ok = true;
   for (int c = 0; c < nchunks; ++c) {
     const int slot = c & 1, c0 = a + c * kRaChunk, n = min(b - c0, kRaChunk);
     if (!ra_wait(&sm.full[slot], (uint32_t)((c >> 1) & 1))) ok = false;
-    // scores: warp w takes positions 4w .. 4w+3 of the chunk
     float s[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -348,49 +347,65 @@ rope_attention_kernel(const float* __restrict__ qkv, const int* __restrict__ pos
     for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
       for (int u = 0; u < 4; ++u) s[u] += __shfl_xor_sync(kFull, s[u], o);
-    if (lane < 4) {
-      const int j = warp * 4 + lane;
-      const float sv = lane == 0 ? s[0] : lane == 1 ? s[1] : lane == 2 ? s[2] : s[3];
-      sm.sc[j] = j < n ? __fmul_rn(sv, scale) : -INFINITY;
-    }
-    __syncthreads();
-    if (warp == 0) {  // running max and sum over the chunk's scores
-      const float sv = sm.sc[lane];
-      float mx = sv;
+    float mx = -INFINITY;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, o));
-      const float m_old = sm.stat[0], m_new = fmaxf(m_old, mx);
-      const float p = (sv == -INFINITY) ? 0.0f : expf(sv - m_new);
-      sm.sc[lane] = p;
-      const float ps = warp_sum(p);
-      if (lane == 0) {
-        const float corr = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
-        sm.stat[0] = m_new;
-        sm.stat[1] = __fadd_rn(__fmul_rn(sm.stat[1], corr), ps);
-        sm.stat[2] = corr;
-      }
+    for (int u = 0; u < 4; ++u) {
+      s[u] = (warp * 4 + u < n) ? __fmul_rn(s[u], scale) : -INFINITY;
+      mx = fmaxf(mx, s[u]);
     }
-    __syncthreads();
-    {
-      float t = 0.0f;
-#pragma unroll 4
-      for (int j = hh * (kRaChunk / 2); j < (hh + 1) * (kRaChunk / 2); ++j) {
-        const float p = sm.sc[j];
-        const float vv = (c0 + j == pos) ? sm.vcur[d] : sm.v[slot][j][d];
-        t = __fadd_rn(t, p != 0.0f ? __fmul_rn(p, vv) : 0.0f);
+    if (mx != -INFINITY) {  // a warp with no position in this chunk keeps its state
+      const float mn = fmaxf(m, mx);
+      const float corr = (m == -INFINITY) ? 0.0f : expf(m - mn);
+      float ps = 0.0f;
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = warp * 4 + u;
+        const float p = (s[u] == -INFINITY) ? 0.0f : expf(s[u] - mn);
+        if (p != 0.0f) {
+          const float* vrow = (c0 + j == pos) ? sm.vcur : sm.v[slot][j];
+          const float4 v4 = reinterpret_cast<const float4*>(vrow)[lane];
+          t.x = __fadd_rn(t.x, __fmul_rn(p, v4.x));
+          t.y = __fadd_rn(t.y, __fmul_rn(p, v4.y));
+          t.z = __fadd_rn(t.z, __fmul_rn(p, v4.z));
+          t.w = __fadd_rn(t.w, __fmul_rn(p, v4.w));
+        }
+        ps = __fadd_rn(ps, p);
       }
-      acc = __fadd_rn(__fmul_rn(acc, sm.stat[2]), t);
+      l = __fadd_rn(__fmul_rn(l, corr), ps);
+      acc.x = __fadd_rn(__fmul_rn(acc.x, corr), t.x);
+      acc.y = __fadd_rn(__fmul_rn(acc.y, corr), t.y);
+      acc.z = __fadd_rn(__fmul_rn(acc.z, corr), t.z);
+      acc.w = __fadd_rn(__fmul_rn(acc.w, corr), t.w);
+      m = mn;
     }
-    __syncthreads();  // slot consumed
+    __syncthreads();  // every warp is done with the slot
     if (tid == 0 && c + 2 < nchunks) issue(c + 2);
   }
   if (!ok && tid == 0) atomicOr(&g_attn_fault, 8u);
-  sm.acc2[hh][d] = acc;
+  if (lane == 0) {
+    sm.wm[warp] = m;
+    sm.wl[warp] = l;
+  }
+  reinterpret_cast<float4*>(sm.wacc[warp])[lane] = acc;
   __syncthreads();
-  if (tid < D) sm.pacc[tid] = __fadd_rn(sm.acc2[0][tid], sm.acc2[1][tid]);
-  if (tid == 0) {
-    sm.stat[3] = nchunks > 0 ? sm.stat[0] : -INFINITY;
-    sm.pl = nchunks > 0 ? sm.stat[1] : 0.0f;
+  // this CTA's partial: the warps merged in warp order
+  if (tid < D) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kRaThreads / 32; ++w) M = fmaxf(M, sm.wm[w]);
+    float L = 0.0f, A = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kRaThreads / 32; ++w) {
+      const float f = (sm.wm[w] == -INFINITY) ? 0.0f : expf(sm.wm[w] - M);
+      L = __fadd_rn(L, __fmul_rn(sm.wl[w], f));
+      A = __fadd_rn(A, __fmul_rn(sm.wacc[w][tid], f));
+    }
+    sm.pacc[tid] = A;
+    if (tid == 0) {
+      sm.stat[3] = M;
+      sm.pl = L;
+    }
   }
   cluster_sync();  // partials of every CTA of the cluster written
   if (rank == 0 && tid < D) {

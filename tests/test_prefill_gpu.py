@@ -217,6 +217,38 @@ def test_prefill_sequences_of_a_batch_are_independent(oracle_lib, cuda_device):
             assert _rel(kb, k1) <= (1e-5 if li == 0 else FLIP_REL_L2), (b, li)
 
 
+def test_prefill_launches_replay_from_a_cuda_graph(cuda_device):
+    """The launches of a prefill synchronise nothing: after one warm-up call of the same
+    size they capture into a CUDA graph, and a replay leaves exactly the state of an eager
+    prefill (next token, logits, cache rows, position)."""
+    cfg, w = _tiny(101)
+    toks = np.random.default_rng(102).integers(0, cfg.vocab, 11)
+    eager = Q8Decoder(cfg, w, device=cuda_device)
+    n_eager = int(eager.prefill(toks).item())
+    dec = Q8Decoder(cfg, w, device=cuda_device)
+    dec.prefill(toks)  # warm-up: workspaces and kernel attributes before the capture
+    dec.reset()
+    tok_d = torch.tensor(toks, dtype=torch.int32, device=cuda_device)
+    stream = torch.cuda.Stream(cuda_device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        dec.logits.zero_()
+        for li in range(cfg.layers):
+            dec.k_cache[li].zero_()
+            dec.v_cache[li].zero_()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            dec._prefill_launches(tok_d, 1, len(toks), 0)
+        graph.replay()
+        torch.cuda.synchronize()
+    assert int(dec.token.item()) == n_eager and int(dec.pos.item()) == len(toks)
+    assert torch.equal(dec.logits, eager.logits)
+    for li in range(cfg.layers):
+        assert torch.equal(dec.k_cache[li][:, :len(toks)], eager.k_cache[li][:, :len(toks)])
+        assert torch.equal(dec.v_cache[li][:, :len(toks)], eager.v_cache[li][:, :len(toks)])
+    del graph
+
+
 def test_prefill_context_limit_and_shapes(cuda_device):
     cfg, w = _tiny(81, max_t=12)
     dec = Q8Decoder(cfg, w, device=cuda_device)
