@@ -1,6 +1,6 @@
 """Benchmark of the B200 Q8_0 quantized linear (decode path, HBM-bound).
 
-Workload (decode rows): the four projection shapes of the shape
+Workload (the shape sweep's decode rows): the four projection shapes of the shape
 sweep -- fused QKV (2048->6144), O (2048->2048), fused gate+up (2048->12288) and
 down (6144->2048) -- at M = 1, for 28 distinct layers of Q8_0 weights (the depth of
 the 2B decoder).  One step = one pass over all 28 x 4 = 112 projections, i.e. the
@@ -286,7 +286,7 @@ def run_case(args) -> None:
 
 
 def run_sweep(torch, L, dev, stream) -> list:
-    """M in {1,4,16,64,256,1024} x the four projection shapes and the
+    """The shape sweep: M in {1,4,16,64,256,1024} x the four projection shapes and the
     real k/v shape (2048 -> 256); device time per call from CUDA-graph replays over weight
     copies spanning twice the L2, and the kernel path that served it."""
     from talechime_b200 import _lib
@@ -307,7 +307,7 @@ def run_sweep(torch, L, dev, stream) -> list:
 
 
 def run_prefill(torch, dist, L, dev, stream, mats, rank: int, world: int, m: int = 4096, reps: int = 3) -> dict:
-    """batched prefill, 4 x 1024 tokens (M = 4096), through the Q8_0
+    """The batched-prefill workload, 4 x 1024 tokens (M = 4096), through the Q8_0
     linears of the 28 layers (qkv, o, gate_up, down per layer; the M > 32 tensor-core
     path): one CUDA graph of the 112 calls, device time per pass (CUDA events), max over
     ranks (one independent replica per GPU).  Attention and the elementwise steps of a
@@ -539,7 +539,7 @@ def run_decoder(torch, dist, dev, rank: int, world: int, prefix: int = 128, step
 
 def run_decoder_prefill(torch, dist, dev, rank: int, world: int, batch: int = 4, tokens: int = 1024,
                         reps: int = 3) -> dict:
-    """BASELINE configs[3] as a decoder pass: the same ~2B Q8_0 decoder prefills `batch`
+    """The batched-prefill workload as a decoder pass: the same ~2B Q8_0 decoder prefills `batch`
     sequences of `tokens` random ids (M = batch * tokens = 4096 rows through every
     linear) with everything of the prompt pass -- embedding, RMSNorms, RoPE + KV append,
     causal attention, residual adds, SwiGLU, final norm, LM head and greedy pick of each
@@ -676,7 +676,7 @@ def main() -> None:
     ap.add_argument("--case", default=None,
                     help="M:K:N -- run one projection shape `--steps` times (profiling), print its timing")
     ap.add_argument("--sweep", action="store_true",
-                    help="also time the BASELINE configs[1] shape sweep (M x {qkv,o,gate_up,down}) into the line")
+                    help="also time the shape sweep (M x {qkv,o,gate_up,down}) into the line")
     ap.add_argument("--profile-prefill", default=None, metavar="B:T",
                     help="ncu helper: one warm-up and one timed prompt pass of B x T tokens (--layers layers)")
     ap.add_argument("--profile-decoder", default=None, choices=["fused", "persistent", "unfused"],

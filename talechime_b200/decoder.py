@@ -1,4 +1,4 @@
-"""Q8_0 decoder (BASELINE configs[2] and [3]: the VoxCPM BaseLM-style Llama decoder):
+"""Q8_0 decoder (the decode and batched-prefill benchmark workloads: the VoxCPM BaseLM-style Llama decoder):
 batch-1 decode steps and a batched prompt pass (``prefill``).
 
 Per layer (crates/voxcpm/src/transformer.rs:107-155): rms_norm -> fused q|k|v Q8_0 linear
@@ -398,7 +398,7 @@ class Q8Decoder:
 
 
 def synthetic_weights(cfg: DecoderConfig, seed: int = 0, device: Optional[torch.device] = None) -> dict:
-    """Random-init Q8_0 weights with BASELINE's distributions (qs uniform in [-127, 127],
+    """Random-init Q8_0 weights with the benchmark's distributions (qs uniform in [-127, 127],
     d = |N(0, 0.02)| / 127 as f16; norm weights 1), numpy on the host or torch uint8 on
     `device` (for the 2 GB full-size model)."""
     def blocks(n, k):

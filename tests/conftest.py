@@ -8,7 +8,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 # Output tolerance of the f32 results against the candle-CPU restatement
-# relative L2 <= 1e-5 and max-abs <= 1e-3 * max|y|.
+# (the parity bar stated for this path): relative L2 <= 1e-5 and max-abs <= 1e-3 * max|y|.
 REL_L2_TOL = 1e-5
 MAX_ABS_FRAC_TOL = 1e-3
 

@@ -1,6 +1,6 @@
 """Parity of q8lin_forward with the candle-CPU oracle at the benchmark's full sizes.
 
-BASELINE configs[1] is a grid of activation rows M in {1, 4, 16, 64, 256, 1024} over the
+The benchmark shape sweep is a grid of activation rows M in {1, 4, 16, 64, 256, 1024} over the
 VoxCPM-style projection shapes qkv 2048->6144, o 2048->2048, gate_up 2048->12288 and
 down 6144->2048, plus the real k/v projection 2048->256
 (crates/voxcpm/src/transformer.rs:119-121,146,148-150, called through Linear::forward,

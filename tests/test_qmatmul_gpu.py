@@ -44,7 +44,7 @@ def test_small_batch_dispatch_shapes(oracle_lib, cuda_device, m, k, n):
 
 
 def test_config0_single_linear(oracle_lib, cuda_device):
-    # x [1,2048], W 2048x2048 Q8_0, seed 0
+    # the single-linear benchmark case: x [1,2048], W 2048x2048 Q8_0, seed 0
     run_case(oracle_lib, cuda_device, 0, 1, 2048, 2048)
 
 
