@@ -16,7 +16,7 @@
 // Layout: units of 16 weight rows x 8 blocks (256 values): per row 256 bytes of int8 and
 // the 8 f16 scales, 272 bytes, so the 16 rows of a unit (4352 bytes) sit 272 bytes apart
 // and ldmatrix reads them without bank conflicts.  Each of the 8 warps streams its
-// own units through a private ring of kMmDepth slots with 16-byte cp.async (L2
+// own units through a private ring of 2 or 3 slots with 16-byte cp.async (L2
 // evict-first); the first slots are issued before the dependency wait, so they overlap the
 // quantization launch.  A CTA owns a contiguous range of 16-row tiles:
 //   - more tiles than ring warps: warp w takes tiles w, w + nw, ..., all K each, and
@@ -43,9 +43,11 @@ constexpr int kMmThreads = kMmWarps * 32;
 constexpr int kUnitBlocks = 8;                          // Q8_0 blocks per unit
 constexpr int kUnitRowBytes = kUnitBlocks * 32 + 16;    // 272: int8 of 8 blocks + their f16 scales
 constexpr int kUnitBytes = 16 * kUnitRowBytes;          // 4352
-constexpr int kMmDepth = 2;
-constexpr int kMmRingWarps = kMmWarps;                  // 8 x 2 x 4352 = 69632 bytes of ring
-constexpr int kMmRingBytes = kMmRingWarps * kMmDepth * kUnitBytes;
+constexpr int kMmRingWarps = kMmWarps;
+// Ring slots per warp: 2 (8 x 2 x 4352 = 69632 bytes, two CTAs per SM where the activations
+// fit beside them) or 3 (104448 bytes, one CTA per SM; the deeper ring keeps a unit's
+// refill off the critical path).
+__host__ __device__ constexpr int ring_bytes(int depth) { return kMmRingWarps * depth * kUnitBytes; }
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 __host__ __device__ constexpr int64_t round_up16(int64_t v) { return (v + 15) / 16 * 16; }
@@ -139,8 +141,10 @@ __device__ __forceinline__ void unit_mma(const MmaArgs& a, uint32_t slot, uint32
   }
 }
 
-template <int NT>
+template <int NT, int DEPTH>
 __global__ void __launch_bounds__(kMmThreads, 2) gemm_q8_0_mma_kernel(const MmaArgs a) {
+  constexpr int kMmDepth = DEPTH;
+  constexpr int kMmRingBytes = ring_bytes(DEPTH);
   extern __shared__ __align__(16) uint8_t smem[];
   const int nb = a.K >> 5;
   const int nkc = (nb + kUnitBlocks - 1) / kUnitBlocks;  // units per tile
@@ -342,15 +346,15 @@ __global__ void __launch_bounds__(kMmThreads, 2) gemm_q8_0_mma_kernel(const MmaA
 size_t up256_mm(size_t v) { return (v + 255) / 256 * 256; }
 int mp_of(int64_t m) { return (int)((m + 15) / 16 * 16); }
 // rings, then the int8 activations (rows K + 16 bytes apart) and their scales [K/32][Mp]
-size_t mma_smem_bytes(int64_t m, int64_t k) {
-  return (size_t)kMmRingBytes + (size_t)round_up16(m * (k + 16)) + (size_t)mp_of(m) * (k / kQK) * sizeof(float);
+size_t mma_smem_bytes(int64_t m, int64_t k, int depth = 2) {
+  return (size_t)ring_bytes(depth) + (size_t)round_up16(m * (k + 16)) + (size_t)mp_of(m) * (k / kQK) * sizeof(float);
 }
 
-template <int NT>
+template <int NT, int DEPTH>
 cudaError_t launch_mma_t(const MmaArgs& a, int device, cudaStream_t s) {
   static int configured[128] = {0};
-  auto fn = gemm_q8_0_mma_kernel<NT>;
-  const size_t smem = mma_smem_bytes(a.M, a.K);
+  auto fn = gemm_q8_0_mma_kernel<NT, DEPTH>;
+  const size_t smem = mma_smem_bytes(a.M, a.K, DEPTH);
   cudaError_t e = ensure_smem((const void*)fn, configured, device, smem, true);
   if (e != cudaSuccess) return e;
   const int tiles = (a.N + 15) / 16;
@@ -371,7 +375,7 @@ cudaError_t launch_mma_t(const MmaArgs& a, int device, cudaStream_t s) {
 
 }  // namespace
 
-// Where the activations fit beside the rings with two CTAs per SM.
+// Where the activations fit beside two-slot rings in one CTA's shared memory.
 bool mma_applies(int64_t m, int64_t k) {
   return m >= 2 && m <= kMmaMaxM && k <= (1 << 20) && mma_smem_bytes(m, k) <= kMmaMaxSmem;
 }
@@ -421,7 +425,14 @@ cudaError_t launch_gemm_mma(const q8lin_weight& w, const float* x, void* workspa
                                              const_cast<float*>(a.dxT), s);
     if (e != cudaSuccess) return e;
   }
-  return m <= 8 ? launch_mma_t<1>(a, w.device, s) : launch_mma_t<2>(a, w.device, s);
+  // Three ring slots where they fit, except where every CTA quantizes x itself (there two
+  // CTAs per SM let the next CTA start streaming during the quantization).  Measured on
+  // B200 (graph-timed, us, 2 -> 3 slots): qkv 2048->6144 M=12 12.5 -> 10.5, M=16 13.6 ->
+  // 12.1; o 2048->2048 M=16 8.7 -> 7.5; gate_up 2048->12288 (x quantized in the kernel)
+  // M=16 18.6 -> 19.4.
+  const bool deep = a.qx != nullptr && mma_smem_bytes(m, w.k, 3) <= kMmaMaxSmem;
+  if (m <= 8) return deep ? launch_mma_t<1, 3>(a, w.device, s) : launch_mma_t<1, 2>(a, w.device, s);
+  return deep ? launch_mma_t<2, 3>(a, w.device, s) : launch_mma_t<2, 2>(a, w.device, s);
 }
 
 }  // namespace q8lin

@@ -126,7 +126,7 @@ cudaError_t launch_quantize_rows_i8t(const float* x, int M, int Mp, int K, int8_
 // small batches on mma.sync int8 tensor cores (gemm_mma.cu): activations quantized once
 // into the workspace, then the weights streamed in 16-row x 256-value units
 constexpr int kMmaMaxM = 16;
-constexpr size_t kMmaMaxSmem = 110 * 1024;
+constexpr size_t kMmaMaxSmem = 220 * 1024;  // rings + staged activations of one CTA
 constexpr int64_t kMmaInKernelMaxValues = 32768;  // M*K the kernel quantizes itself ...
 constexpr int64_t kMmaInKernelMinN = 8192;        // ... for weights of at least this many rows
 bool mma_applies(int64_t m, int64_t k);

@@ -121,8 +121,8 @@ def test_python_surface_rejects_cpu_device():
     (11, 2048, 12288, "small_batch_dp4a"),
     (12, 2048, 2048, "small_batch_mma"),  # 12 <= M <= 16 where x fits in shared memory
     (16, 2048, 12288, "small_batch_mma"),
-    (16, 4096, 2048, "int8_tc"),          # ... not at K = 4096 (x does not fit)
-    (12, 6144, 2048, "int8_tc"),
+    (16, 4096, 2048, "small_batch_mma"),  # x fits beside the rings in one CTA up to K ~ 8K
+    (12, 6144, 2048, "small_batch_mma"),
     (17, 2048, 2048, "int8_tc"),
     (32, 6144, 2048, "int8_tc"),
     (33, 2048, 2048, "f16_tc"),
